@@ -1,0 +1,505 @@
+"""Benchmark of the B200 Linear hot path (one JSON line on rank 0).
+
+Headline: the W8A16 decode GEMV sweep, M=1, over the
+five Qwen2.5-0.5B shapes K->N = 896->896, 896->128, 896->4864, 4864->896,
+896->151936, reported as GB/s of algorithmic bytes (int8 weights + BF16
+scales + BF16 x, y and bias) per second.  One *step* = `passes` passes over
+the five shapes (one GEMV call per shape per pass), replayed from a CUDA
+graph.  Each shape cycles through a ring of distinct weight copies holding
+more than 4x the L2 size between two uses of the same copy, so every launch
+streams its weights from HBM (inputs larger than L2; no L2 flush needed).
+
+Also reported: the same sweep in BF16, the prefill GEMM sweep,
+the roofline of the dominant kernel, the reference's CPU FP32 path on the
+host cores, and `e2e` = the same metric through the public Python API with
+host (pinned) inputs/outputs copied inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs an independent replica of the sweep on
+its own GPU (batch-1 decode does not shard): weak scaling, value = sum of the
+ranks' bytes / max over ranks of the device time.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "qwen2.5-jetson-inference_b200")
+SHAPES = [(896, 896), (896, 128), (896, 4864), (4864, 896), (896, 151936)]  # K -> N
+PREFILL_M = [32, 128, 512, 2048, 8192]
+BIAS_SHAPES = {(896, 896), (896, 128)}  # q/k/v-like shapes carry a bias
+
+
+def load_pkg():
+    name = "qwen25_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(
+        name, os.path.join(PKG_DIR, "__init__.py"), submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def w8_bytes(n, k, bias):
+    groups = (k + 63) // 64
+    return n * k + 2 * n * groups + 2 * k + 2 * n + (2 * n if bias else 0)
+
+
+def bf16_bytes(n, k, bias):
+    return 2 * n * k + 2 * k + 2 * n + (2 * n if bias else 0)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.path is None or not os.path.exists(self.path):
+            return None
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------- workload
+class GemvSweep:
+    """Weight rings + inputs for the five decode shapes in one precision."""
+
+    def __init__(self, b200, w8, passes, device, seed=1234):
+        self.b200, self.w8, self.passes, self.device = b200, w8, passes, device
+        l2 = torch.cuda.get_device_properties(device).L2_cache_size
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.items = []
+        for (k, n) in SHAPES:
+            has_bias = (k, n) in BIAS_SHAPES
+            w = torch.randn(n, k, generator=gen, device=device) * 0.02
+            nbytes = w8_bytes(n, k, has_bias) if w8 else bf16_bytes(n, k, has_bias)
+            ring = max(2, min(passes, math.ceil(4 * l2 / nbytes)))
+            if w8:
+                q, s = b200.quantize_groupwise(w)
+                copies = [(q.clone(), s.clone()) for _ in range(ring)]
+            else:
+                wb = w.to(torch.bfloat16)
+                copies = [(wb.clone(), None) for _ in range(ring)]
+            del w
+            x = torch.randn(k, generator=gen, device=device).to(torch.bfloat16)
+            bias = (torch.randn(n, generator=gen, device=device) * 0.02).to(torch.bfloat16) \
+                if has_bias else None
+            y = torch.empty(n, dtype=torch.bfloat16, device=device)
+            self.items.append(dict(k=k, n=n, copies=copies, x=x, bias=bias, y=y,
+                                   bytes=nbytes))
+        self.bytes_per_pass = sum(it["bytes"] for it in self.items)
+
+    def call(self, it, copy_index, x=None, y=None):
+        w, s = it["copies"][copy_index % len(it["copies"])]
+        x = it["x"] if x is None else x
+        y = it["y"] if y is None else y
+        if self.w8:
+            self.b200.gemv_w8a16(w, s, 64, it["bias"], x, y, it["n"], it["k"])
+        else:
+            self.b200.gemv_bf16(w, it["bias"], x, y, it["n"], it["k"])
+
+    def step(self):
+        for p in range(self.passes):
+            for it in self.items:
+                self.call(it, p)
+
+
+def capture(fn):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # warm (also builds any lazily set kernel attributes)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, reps, warmup):
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / 1e3 / reps
+
+
+def per_shape(sweep, calls=200):
+    out = []
+    for it in sweep.items:
+        g = capture(lambda it=it: [sweep.call(it, i) for i in range(calls)])
+        t = time_graph(g, 5, 2) / calls
+        out.append({"k": it["k"], "n": it["n"], "bytes": it["bytes"],
+                    "us": round(t * 1e6, 3), "gbs": round(it["bytes"] / t / 1e9, 1)})
+        del g
+    return out
+
+
+def gemm_sweep(b200, device, reps=10):
+    """M x five shapes x {W8A16, BF16}; TFLOP/s with CUDA events."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99)
+    res = []
+    for (k, n) in SHAPES:
+        w = torch.randn(n, k, generator=gen, device=device) * 0.02
+        q, s = b200.quantize_groupwise(w)
+        wb = w.to(torch.bfloat16)
+        del w
+        bias = (torch.randn(n, generator=gen, device=device) * 0.02).to(torch.bfloat16) \
+            if (k, n) in BIAS_SHAPES else None
+        for m in PREFILL_M:
+            x = torch.randn(m, k, generator=gen, device=device).to(torch.bfloat16)
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+            for w8 in (True, False):
+                def run():
+                    if w8:
+                        b200.gemm_w8a16(q, s, 64, bias, x, y, m, n, k)
+                    else:
+                        b200.gemm_bf16(wb, bias, x, y, m, n, k)
+                for _ in range(3):
+                    run()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record()
+                for _ in range(reps):
+                    run()
+                e1.record()
+                torch.cuda.synchronize()
+                t = e0.elapsed_time(e1) / 1e3 / reps
+                res.append({"w8": w8, "m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
+                            "tflops": round(2.0 * m * n * k / t / 1e12, 1)})
+            del x, y
+        del q, s, wb
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------ CPU reference
+def cpu_reference_sample(steps, warmup, budget_s=12.0):
+    """Reference src/cpu_ops.cpp linear_fp32 (OpenBLAS sgemv, FP32 weights) on
+    the same five shapes; value in the same metric (W8A16 algorithmic bytes
+    of the sweep / time).  Returns (value_gbs, cores, sample text)."""
+    sys.path.insert(0, REPO)
+    from oracle import oracle as O
+    lib = O.ref_cpu()
+    kind = "reference"
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(5)
+    mats = []
+    for (k, n) in SHAPES:
+        w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+        x = rng.standard_normal(k, dtype=np.float32)
+        b = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)) \
+            if (k, n) in BIAS_SHAPES else None
+        mats.append((w, b, x, w8_bytes(n, k, b is not None)))
+    if lib is not None:
+        lib.ref_cpu_set_threads(cores)
+        fn = O.ref_cpu_linear
+    else:  # the oracle restatement (single-threaded per row block)
+        kind = "port"
+        fn = lambda w, b, x: O.linear_bf16(O.f32_to_bf16(w), None if b is None
+                                           else O.f32_to_bf16(b), O.f32_to_bf16(x))
+    for _ in range(max(1, warmup)):
+        for (w, b, x, _) in mats:
+            fn(w, b, x)
+    t0 = time.perf_counter()
+    passes = 0
+    total = 0
+    while True:
+        for (w, b, x, nb) in mats:
+            fn(w, b, x)
+            total += nb
+        passes += 1
+        if passes >= steps or time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return total / dt / 1e9, cores, kind, (
+        f"{passes} passes of the 5-shape decode sweep, reference CPU FP32 "
+        f"linear_fp32 (OpenBLAS sgemv) on FP32 weights, {dt:.2f} s")
+
+
+# ------------------------------------------------------------------- main
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+METRIC = "W8A16 decode GEMV GB/s (5 Qwen2.5-0.5B shapes, M=1)"
+UNIT = "GB/s"
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    value, cores, kind, sample = cpu_reference_sample(args.steps, args.warmup)
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)",
+            "config": {"workload": "decode GEMV sweep K->N " +
+                       ",".join(f"{k}->{n}" for k, n in SHAPES), "m": 1},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores,
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--passes", type=int, default=100, help="sweep passes per step")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the GEMM sweep")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world, rank, local = init_dist()
+    device = torch.device("cuda", local)
+    b200 = load_pkg()
+    hbm, tf_burst, tf_sust, peak_kind = measured_peaks()
+
+    # ---- headline: W8A16 GEMV sweep, graph-replayed steps
+    sweep = GemvSweep(b200, True, args.passes, device)
+    g = capture(sweep.step)
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    local_s = e0.elapsed_time(e1) / 1e3
+    t_max = max_over_ranks(local_s, world)
+    step_bytes = sweep.bytes_per_pass * args.passes
+    total_bytes = sum_over_ranks(step_bytes * args.steps, world)
+    value = total_bytes / t_max / 1e9
+    launches = len(SHAPES) * args.passes * args.steps
+    clocks = clk.summary()
+    del g
+
+    # ---- roofline of the dominant kernel (W8 GEMV on the 896->151936 shape)
+    big = sweep.items[-1]
+    calls = 40
+    gb = capture(lambda: [sweep.call(big, i) for i in range(calls)])
+    t_big = time_graph(gb, 5, 2) / calls
+    del gb
+    achieved = big["bytes"] / t_big / 1e9
+    traffic = None
+    prof = os.path.join(REPO, "profiles", "gemv_w8a16_896x151936.md")
+    if os.path.exists(prof):
+        for line in open(prof):
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1].strip())
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
+                "peak_kind": peak_kind, "kernel": "gemv_stream_kernel<W8> 896->151936",
+                "algorithmic_bytes_per_launch": big["bytes"],
+                "us_per_launch": round(t_big * 1e6, 2)}
+    shapes_w8 = per_shape(sweep)
+    e2e = None
+    if rank == 0 or world > 1:
+        # ---- e2e: public API, pinned host x in, host y out, every step.
+        xs_host = [it["x"].cpu().pin_memory() for it in sweep.items]
+        ys_host = [torch.empty(it["n"], dtype=torch.bfloat16).pin_memory()
+                   for it in sweep.items]
+        xs_dev = [torch.empty_like(it["x"]) for it in sweep.items]
+        e2e_steps = max(1, args.steps)
+        h2d = sum(2 * it["k"] for it in sweep.items)
+        d2h = sum(2 * it["n"] for it in sweep.items)
+
+        def e2e_step(step):
+            for i, it in enumerate(sweep.items):
+                xs_dev[i].copy_(xs_host[i], non_blocking=True)
+                sweep.call(it, step, x=xs_dev[i])
+                ys_host[i].copy_(it["y"], non_blocking=True)
+        for s in range(2):
+            e2e_step(s)
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        for s in range(e2e_steps):
+            e2e_step(s)
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+        e2e_bytes = sum_over_ranks(sweep.bytes_per_pass * e2e_steps, world)
+        e2e = {"value": round(e2e_bytes / e2e_s / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "note": "one pass of the 5-shape sweep per step through the Python "
+                       "API (ctypes -> C ABI), x copied from pinned host memory and y "
+                       "read back each step; host wall clock, max over ranks"}
+    del sweep
+    torch.cuda.empty_cache()
+
+    sweep16 = GemvSweep(b200, False, min(args.passes, 20), device)
+    shapes_bf16 = per_shape(sweep16)
+    del sweep16
+    torch.cuda.empty_cache()
+
+    gemm = None
+    if not args.no_gemm:
+        gemm = gemm_sweep(b200, device)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, kind, sample = cpu_reference_sample(10 ** 9, 1, budget_s=12.0)
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": kind,
+               "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_max / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xbf16->f32", "data": "synthetic (seeded N(0,0.02) weights "
+            "quantised by the exporter rule, N(0,1) BF16 x)",
+            "config": {"workload": "decode GEMV sweep (configs[1]) K->N " +
+                       ",".join(f"{k}->{n}" for k, n in SHAPES),
+                       "m": 1, "passes_per_step": args.passes, "group_size": 64,
+                       "l2": "inputs larger than L2: per-shape ring of weight copies, "
+                             ">4x L2 between reuses",
+                       "parallelism": f"replicas x{world}"},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "sweep_w8a16": shapes_w8,
+            "sweep_bf16": shapes_bf16,
+            "gemm_sweep": gemm,
+            "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf_burst,
+                      "bf16_tflops_sustained": tf_sust, "kind": peak_kind},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,139 @@
+/*
+ * b200_linear.h - C ABI of the B200 (sm_100a) Linear-layer kernels.
+ *
+ * Drop-in boundary for the reference engine's CUDA Linear interface
+ * (reference include/infer/cuda_ops.hpp:24-55,102-103; implemented there in
+ * src/cuda/kernels.cu:1540-1704).  Every entry point takes raw device
+ * pointers, sizes and a CUDA stream; nothing here allocates device memory,
+ * synchronises the stream, or keeps state between calls (except the
+ * device-side error word read by b200_device_status).  All work is enqueued
+ * asynchronously on `stream`, exactly like the reference functions.
+ *
+ * Layouts (reference conventions, src/qwen2.cpp:231-330):
+ *   weight  [out_features, in_features] row-major (BF16 bits, or int8)
+ *   scales  [out_features, ceil(in_features / 64)] BF16 bits (W8A16)
+ *   input   [tokens, in_features] row-major BF16 bits
+ *   output  [tokens, out_features] row-major BF16 bits
+ *   bias    [out_features] BF16 bits, or NULL
+ * BF16 values are passed as uint16_t bit patterns.  Accumulation is FP32 and
+ * every output is rounded to BF16 round-to-nearest-even.
+ *
+ * Return value: B200_OK (0); a negative B200_ERR_* code for an argument the
+ * kernels do not accept (the reference throws infer::Error in those cases);
+ * or a positive cudaError_t value from the launch.
+ */
+#ifndef B200_LINEAR_H_
+#define B200_LINEAR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t (struct CUstream_st*), spelled without the CUDA
+ * headers so that C/FFI callers need none.  NULL = the legacy default stream. */
+typedef struct CUstream_st* b200_stream_t;
+
+#define B200_OK 0
+#define B200_ERR_INVALID_ARGUMENT (-1) /* NULL pointer, negative size */
+#define B200_ERR_GROUP_SIZE (-2)       /* W8A16 group_size other than 64 */
+#define B200_ERR_WORKSPACE (-3)        /* workspace missing or too small */
+#define B200_ERR_TOO_LARGE (-4)        /* size beyond a stated limit */
+#define B200_ERR_NCCL (-5)             /* NCCL call failed (sharded ops) */
+
+/* Device-side error codes recorded by kernels whose bounded waits expired. */
+#define B200_DEVICE_OK 0
+#define B200_DEVICE_TIMEOUT_PIPELINE 1 /* GEMM smem pipeline wait expired */
+#define B200_DEVICE_TIMEOUT_ACCUM 2    /* GEMM TMEM accumulator wait expired */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int b200_version(void);
+
+/* Human-readable text for a status returned by any b200_* function. */
+const char* b200_status_string(int status);
+
+/* Reads (and if clear != 0, resets) the device-side error word of the
+ * current device.  Returns a B200_DEVICE_* code, or a negative B200_ERR_* /
+ * the negated cudaError_t if the read itself failed.  Synchronises the
+ * current device. */
+int b200_device_status(int clear);
+
+/* Decode GEMV, BF16 weights: output[n] = bf16(sum_k W[n,k] x[k] + b[n]).
+ * Replaces infer::cuda::gemv_bf16 (reference include/infer/cuda_ops.hpp:24-26,
+ * src/cuda/kernels.cu:1540-1564).  Any out_features/in_features >= 0 and any
+ * 2-byte alignment; the vectorised path needs in_features % 8 == 0 and
+ * 16-byte aligned weight/input. */
+int b200_gemv_bf16(const uint16_t* weight, const uint16_t* bias,
+                   const uint16_t* input, uint16_t* output, int out_features,
+                   int in_features, b200_stream_t stream);
+
+/* Decode GEMV, W8A16 (group-64 INT8 weights, BF16 scales):
+ * output[n] = bf16(sum_k float(q[n,k]) * s[n,k/64] * x[k] + b[n]).
+ * Replaces infer::cuda::gemv_w8a16 (reference include/infer/cuda_ops.hpp:45-48,
+ * src/cuda/kernels.cu:1627-1655).  group_size must be 64
+ * (B200_ERR_GROUP_SIZE otherwise, checked before any pointer, as the
+ * reference does at src/cuda/kernels.cu:1631). */
+int b200_gemv_w8a16(const int8_t* weight, const uint16_t* scales,
+                    int group_size, const uint16_t* bias,
+                    const uint16_t* input, uint16_t* output, int out_features,
+                    int in_features, b200_stream_t stream);
+
+/* Prefill GEMM, BF16 weights: Y[m,n] = bf16(sum_k X[m,k] W[n,k] + b[n]).
+ * Replaces infer::cuda::gemm_bf16 (reference include/infer/cuda_ops.hpp:32-35,
+ * src/cuda/kernels.cu:1600-1625).  Tensor-core (tcgen05) path when
+ * in_features % 8 == 0 and weight/input/output are 16-byte aligned;
+ * otherwise a CUDA-core path with the same results within tolerance. */
+int b200_gemm_bf16(const uint16_t* weight, const uint16_t* bias,
+                   const uint16_t* input, uint16_t* output, int tokens,
+                   int out_features, int in_features, b200_stream_t stream);
+
+/* Prefill GEMM, W8A16: Y[m,n] = bf16(sum_k X[m,k] bf16(q[n,k] s[n,k/64]) + b[n])
+ * (the dequantised weight is rounded to BF16 before the multiply, as the
+ * reference's tensor-core GEMM does, src/cuda/kernels.cu:1075-1094).
+ * Replaces infer::cuda::gemm_w8a16 (reference include/infer/cuda_ops.hpp:49-53,
+ * src/cuda/kernels.cu:1657-1684).  group_size must be 64. */
+int b200_gemm_w8a16(const int8_t* weight, const uint16_t* scales,
+                    int group_size, const uint16_t* bias,
+                    const uint16_t* input, uint16_t* output, int tokens,
+                    int out_features, int in_features, b200_stream_t stream);
+
+/* Bytes of workspace b200_lm_head_* need, split as the reference splits it:
+ * ceil(vocab/8) floats followed by ceil(vocab/8) ints
+ * (reference src/qwen2.cpp:193-198).  The kernels use at most that much. */
+size_t b200_lm_head_workspace_bytes(int vocab, int in_features);
+
+/* Fused LM head: writes all BF16 logits[v] = bf16(sum_k W[v,k] x[k] + b[v])
+ * and *argmax = the index of the largest BF16-rounded logit, lowest index on
+ * ties.  block_max_value / block_max_index are caller workspace of
+ * ceil(vocab/8) entries each.  Replaces infer::cuda::lm_head_bf16 (reference
+ * include/infer/cuda_ops.hpp:40-43, src/cuda/kernels.cu:1566-1579). */
+int b200_lm_head_bf16(const uint16_t* weight, const uint16_t* bias,
+                      const uint16_t* input, uint16_t* logits,
+                      float* block_max_value, int* block_max_index,
+                      int* argmax, int vocab, int in_features,
+                      b200_stream_t stream);
+
+/* W8A16 form of the fused LM head (GEMV dequant arithmetic), for the
+ * synthetic 896->151936 INT8 shape.  The reference has no INT8 LM head; its
+ * equivalent is gemv_w8a16 followed by argmax_bf16
+ * (src/cuda/kernels.cu:1627-1655, 326-356). */
+int b200_lm_head_w8a16(const int8_t* weight, const uint16_t* scales,
+                       int group_size, const uint16_t* bias,
+                       const uint16_t* input, uint16_t* logits,
+                       float* block_max_value, int* block_max_index,
+                       int* argmax, int vocab, int in_features,
+                       b200_stream_t stream);
+
+/* Argmax over n BF16 values, lowest index on ties; 0 when n <= 0.
+ * Replaces infer::cuda::argmax_bf16 (reference include/infer/cuda_ops.hpp:102-103,
+ * src/cuda/kernels.cu:326-356, 1534-1538). */
+int b200_argmax_bf16(const uint16_t* values, int n, int* output,
+                     b200_stream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* B200_LINEAR_H_ */

@@ -1,0 +1,613 @@
+// Prefill GEMM on the 5th-generation tensor cores (sm_100a):
+//   Y[M,N] = bf16( X[M,K] . W[N,K]^T + b[N] ),  FP32 accumulation in TMEM.
+//
+// Replaces the reference's WMMA GEMMs gemm_bf16 / gemm_w8a16
+// (src/cuda/kernels.cu:605-951, 1096-1322, dispatch 1600-1684).
+//
+// Structure (one persistent CTA per SM, warp-specialised):
+//   warp 0        TMA producer: X tile(s) [128 x 64] BF16 (128-byte swizzle)
+//                 and the W tile [BN x 64] (BF16 swizzled, or raw INT8)
+//                 into a ring of shared-memory stages (mbarrier complete_tx).
+//   warp 1        TMEM allocator and the single-thread tcgen05.mma issuer:
+//                 MSUB x (M=128, N=BN, K=16) MMAs per 16-wide k step, FP32
+//                 accumulators in TMEM, double-buffered across tiles;
+//                 tcgen05.commit releases smem stages and hands finished
+//                 accumulators to the epilogue.
+//   warps 4..7    epilogue: tcgen05.ld 32 columns at a time, + bias, BF16
+//                 round-to-nearest-even, store.
+//   warps 8..15   (W8A16 only) dequantisers: raw INT8 tile -> bf16(q * s)
+//                 written straight into the 128-byte-swizzled K-major layout
+//                 the MMA reads, then fence.proxy.async and an mbarrier
+//                 arrive.  One BK=64 k-block is exactly one quantisation
+//                 group, so each W row needs one scale per stage.
+//
+// The BF16 rounding of q*s matches the reference's tensor-core GEMM
+// (src/cuda/kernels.cu:1084-1092): the product of an int8 and a BF16 scale
+// is exact in FP32 and fma.rn.bf16x2(q, s, -0) rounds it once.
+//
+// Every mbarrier wait is bounded (kWaitTimeoutNs); on expiry the CTA records
+// B200_DEVICE_TIMEOUT_* in g_device_status, raises a shared abort flag so
+// the other roles stop waiting, frees its TMEM and returns.
+//
+// No TMA multicast is used (this kernel also runs on every rank of the
+// column-sharded GEMM).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace b200 {
+
+__device__ int g_device_status = 0;
+
+cudaError_t read_device_status(int* value, bool clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpyFromSymbol(value, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return e;
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+  }
+  return e;
+}
+
+namespace {
+
+constexpr int kBK = 64;                    // K per stage = one W8 group
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar,
+                                                      uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   bar),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void record_device_error(int code) {
+  atomicCAS(&g_device_status, 0, code);
+}
+
+// Bounded wait on the phase with the given parity.  Returns false (and makes
+// sure the abort flag is raised) if the CTA is aborting or the wait expired.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort_flag,
+                                          int error_code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - start > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      record_device_error(error_code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap,
+                                            int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::"
+      "complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
+// layout written by TMA SWIZZLE_128B: rows of 128 bytes, 8-row (1024-byte)
+// swizzle atoms stacked along M/N (stride byte offset 1024), descriptor
+// version 1 (sm_100), layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;              // leading byte offset (unused here)
+  d |= uint64_t(1024 >> 4) << 32;      // stride byte offset
+  d |= uint64_t(1) << 46;              // version
+  d |= uint64_t(2) << 61;              // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D=F32, A=B=BF16, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) |
+         (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc,
+                                         uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
+      "[%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// --------------------------------------------------------------- the kernel
+template <bool kW8, int kMSub, int kBN>
+struct Cfg {
+  static constexpr int kBM = 128 * kMSub;
+  static constexpr int kABytes = 128 * kBK * 2;          // one 128-row sub-tile
+  static constexpr int kBBytes = kBN * kBK * 2;          // BF16 B tile
+  static constexpr int kQBytes = kW8 ? kBN * kBK : 0;    // raw INT8 B tile
+  static constexpr int kStageBytes = kMSub * kABytes + kBBytes + kQBytes;
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 6
+                                     ? 6
+                                     : (200 * 1024) / kStageBytes;
+  static constexpr int kAccCols = kMSub * kBN;           // fp32 columns / tile
+  static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kAccBufs * kAccCols;  // power of two
+  static constexpr int kDqWarps = kW8 ? 8 : 0;
+  static constexpr int kWarps = 8 + kDqWarps;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kTxBytes = kMSub * kABytes + (kW8 ? kQBytes : kBBytes);
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static_assert(kTmemCols == 32 || kTmemCols == 64 || kTmemCols == 128 ||
+                    kTmemCols == 256 || kTmemCols == 512,
+                "TMEM allocation must be a power of two >= 32");
+  static_assert(kBN % 32 == 0 && kBN >= 32 && kBN <= 256, "bad BN");
+};
+
+struct TileIter {
+  int tile, kb;
+};
+
+template <bool kW8, int kMSub, int kBN>
+__global__ void __launch_bounds__(Cfg<kW8, kMSub, kBN>::kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+               const __grid_constant__ CUtensorMap tmap_w,
+               const bf16* __restrict__ scales, const bf16* __restrict__ bias,
+               bf16* __restrict__ out, int m, int n, int k) {
+  using C = Cfg<kW8, kMSub, kBN>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte alignment for the swizzle atoms.
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  // bars: full[S], dq_full[S], empty[S], acc_full[2], acc_empty[2]
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_dq = bar_full + 8 * C::kStages;
+  const uint32_t bar_empty = bar_dq + 8 * C::kStages;
+  const uint32_t bar_acc_full = bar_empty + 8 * C::kStages;
+  const uint32_t bar_acc_empty = bar_acc_full + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * C::kStages + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (m + C::kBM - 1) / C::kBM;
+  const int num_n = (n + kBN - 1) / kBN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (k + kBK - 1) / kBK;
+  const int groups = (k + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_dq + 8 * s, C::kDqWarps > 0 ? C::kDqWarps * 32 : 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_acc_full + 8 * a, 1);
+      mbar_init(bar_acc_empty + 8 * a, 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile(
+        "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+            smem_u32(tmem_slot)),
+        "r"(C::kTmemCols)
+        : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::
+                     : "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile % num_m;
+        const int nb = tile / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                         B200_DEVICE_TIMEOUT_PIPELINE))
+            goto producer_done;
+          unsigned char* st = stage_base + stage * C::kStageBytes;
+          const uint32_t fb = bar_full + 8 * stage;
+          mbar_arrive_expect_tx(fb, C::kTxBytes);
+#pragma unroll
+          for (int s = 0; s < kMSub; ++s) {
+            tma_load_2d(smem_u32(st + s * C::kABytes), &tmap_x, kb * kBK,
+                        mb * C::kBM + s * 128, fb);
+          }
+          unsigned char* wdst = st + kMSub * C::kABytes + (kW8 ? C::kBBytes : 0);
+          tma_load_2d(smem_u32(wdst), &tmap_w, kb * kBK, nb * kBN, fb);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+        const int buf = C::kAccBufs == 2 ? (it & 1) : 0;
+        const uint32_t use = C::kAccBufs == 2 ? ((it >> 1) & 1) : (it & 1);
+        if (!mbar_wait(bar_acc_empty + 8 * buf, use ^ 1, abort_flag,
+                       B200_DEVICE_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t d_base = tmem_base + uint32_t(buf * C::kAccCols);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const uint32_t ready = kW8 ? bar_dq + 8 * stage : bar_full + 8 * stage;
+          if (!mbar_wait(ready, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          unsigned char* st = stage_base + stage * C::kStageBytes;
+          const uint32_t b_addr = smem_u32(st + kMSub * C::kABytes);
+#pragma unroll
+          for (int s = 0; s < kMSub; ++s) {
+            const uint32_t a_addr = smem_u32(st + s * C::kABytes);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              mma_bf16(d_base + uint32_t(s * kBN), desc_sw128(a_addr + kk * 32),
+                       desc_sw128(b_addr + kk * 32), idesc,
+                       (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(bar_empty + 8 * stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(bar_acc_full + 8 * buf);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter
+    const bool vec_ok =
+        (n % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int mb = tile % num_m;
+      const int nb = tile / num_m;
+      const int buf = C::kAccBufs == 2 ? (it & 1) : 0;
+      const uint32_t use = C::kAccBufs == 2 ? ((it >> 1) & 1) : (it & 1);
+      if (!mbar_wait(bar_acc_full + 8 * buf, use, abort_flag,
+                     B200_DEVICE_TIMEOUT_ACCUM))
+        break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int s = 0; s < kMSub; ++s) {
+        const int row = mb * C::kBM + s * 128 + q * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + (uint32_t(q * 32) << 16) +
+                        uint32_t(buf * C::kAccCols + s * kBN + c0),
+                    r);
+          const int col0 = nb * kBN + c0;
+          if (row < m && col0 < n) {
+            bf16* dst = out + size_t(row) * n + col0;
+            if (vec_ok && col0 + 32 <= n) {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                uint32_t packed[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = v * 8 + e * 2;
+                  float f0 = __uint_as_float(r[j]);
+                  float f1 = __uint_as_float(r[j + 1]);
+                  if (bias) {
+                    f0 += __bfloat162float(bias[col0 + j]);
+                    f1 += __bfloat162float(bias[col0 + j + 1]);
+                  }
+                  const bf162 h = __floats2bfloat162_rn(f0, f1);
+                  packed[e] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                reinterpret_cast<uint4*>(dst)[v] =
+                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col0 + j < n) {
+                  float f = __uint_as_float(r[j]);
+                  if (bias) f += __bfloat162float(bias[col0 + j]);
+                  dst[j] = __float2bfloat16_rn(f);
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_acc_empty + 8 * buf);
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------- dequantiser
+    if constexpr (kW8) {
+    const int dt = threadIdx.x - 8 * 32;        // 0 .. 255
+    constexpr int kItems = kBN * 4;             // (row, 16-byte chunk) pairs
+    constexpr int kPerThread = kItems / (C::kDqWarps * 32);
+    static_assert(kItems % (C::kDqWarps * 32) == 0, "dequant split");
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int nb = tile / num_m;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        // Scales of this k-block for my rows (issued before the wait).
+        float sc[kPerThread];
+#pragma unroll
+        for (int p = 0; p < kPerThread; ++p) {
+          const int item = dt + p * (C::kDqWarps * 32);
+          const int row = nb * kBN + (item >> 2);
+          sc[p] = row < n ? __bfloat162float(scales[size_t(row) * groups + kb])
+                          : 0.0f;
+        }
+        if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag,
+                       B200_DEVICE_TIMEOUT_PIPELINE))
+          goto dequant_done;
+        unsigned char* st = stage_base + stage * C::kStageBytes;
+        unsigned char* bt = st + kMSub * C::kABytes;
+        const unsigned char* qt = bt + C::kBBytes;
+#pragma unroll
+        for (int p = 0; p < kPerThread; ++p) {
+          const int item = dt + p * (C::kDqWarps * 32);
+          const int r = item >> 2;
+          const int j = item & 3;
+          const uint4 raw = *reinterpret_cast<const uint4*>(qt + r * kBK + j * 16);
+          const bf16 sb = __float2bfloat16_rn(sc[p]);  // exact: sc is BF16
+          const bf162 s2 = __halves2bfloat162(sb, sb);
+          const bf162 neg0 = __halves2bfloat162(__ushort_as_bfloat16(0x8000),
+                                                __ushort_as_bfloat16(0x8000));
+          uint32_t outw[8];
+          const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t b = words[wi] ^ 0x80808080u;
+            const uint32_t f0 = __float_as_uint(s8_to_f32_biased<0>(b));
+            const uint32_t f1 = __float_as_uint(s8_to_f32_biased<1>(b));
+            const uint32_t f2 = __float_as_uint(s8_to_f32_biased<2>(b));
+            const uint32_t f3 = __float_as_uint(s8_to_f32_biased<3>(b));
+            // q has <= 8 significant bits, so its BF16 is the top half.
+            uint32_t q01 = __byte_perm(f0, f1, 0x7632);
+            uint32_t q23 = __byte_perm(f2, f3, 0x7632);
+            bf162 d01 = __hfma2(*reinterpret_cast<bf162*>(&q01), s2, neg0);
+            bf162 d23 = __hfma2(*reinterpret_cast<bf162*>(&q23), s2, neg0);
+            outw[2 * wi] = *reinterpret_cast<uint32_t*>(&d01);
+            outw[2 * wi + 1] = *reinterpret_cast<uint32_t*>(&d23);
+          }
+          // 16 BF16 = 16-byte chunks 2j and 2j+1 of row r, 128B-swizzled.
+          unsigned char* rowp = bt + (r >> 3) * 1024 + (r & 7) * 128;
+          const int c0 = (2 * j) ^ (r & 7);
+          const int c1 = (2 * j + 1) ^ (r & 7);
+          *reinterpret_cast<uint4*>(rowp + c0 * 16) =
+              make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          *reinterpret_cast<uint4*>(rowp + c1 * 16) =
+              make_uint4(outw[4], outw[5], outw[6], outw[7]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bar_dq + 8 * stage);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  dequant_done:;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
+                     tmem_base),
+                 "r"(C::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault,
+                                &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+bool make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+               int elem_bytes, int inner, int outer, int box_inner,
+               int box_outer, CUtensorMapSwizzle swizzle) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
+  cuuint64_t strides[1] = {cuuint64_t(inner) * elem_bytes};
+  cuuint32_t box[2] = {cuuint32_t(box_inner), cuuint32_t(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int count = 148;
+  cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+  return count;
+}
+
+template <bool kW8, int kMSub, int kBN>
+cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
+                       const bf16* input, bf16* output, int m, int n, int k,
+                       cudaStream_t stream) {
+  using C = Cfg<kW8, kMSub, kBN>;
+  CUtensorMap tx, tw;
+  if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (kW8) {
+    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, kBN,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK,
+                   kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  }
+  auto kernel = gemm_tc_kernel<kW8, kMSub, kBN>;
+  cudaError_t e = cudaFuncSetAttribute(
+      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int tiles = ((m + C::kBM - 1) / C::kBM) * ((n + kBN - 1) / kBN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, scales, bias,
+                                                        output, m, n, k);
+  return cudaGetLastError();
+}
+
+bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(bool w8, const void* weight, const void* input,
+                       const void* output, int m, int n, int k) {
+  (void)output;
+  if (m <= 0 || n <= 0 || k <= 0) return false;
+  if (k % (w8 ? 16 : 8) != 0) return false;  // TMA row stride: 16-byte multiple
+  if (!aligned16(weight) || !aligned16(input)) return false;
+  return get_encode_fn() != nullptr;
+}
+
+// Tile-shape choice: the largest tile that still gives every SM work.
+cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
+                           const bf16* bias, const bf16* input, bf16* output,
+                           int m, int n, int k, cudaStream_t stream) {
+  const long long sms = sm_count();
+  const long long tiles_256x128 = ((m + 255) / 256) * (long long)((n + 127) / 128);
+  const long long tiles_128x128 = ((m + 127) / 128) * (long long)((n + 127) / 128);
+  if (w8) {
+    if (tiles_256x128 >= sms)
+      return launch_cfg<true, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
+    if (tiles_128x128 >= sms / 2)
+      return launch_cfg<true, 1, 128>(weight, scales, bias, input, output, m, n, k, stream);
+    return launch_cfg<true, 1, 64>(weight, scales, bias, input, output, m, n, k, stream);
+  }
+  if (tiles_256x128 >= sms)
+    return launch_cfg<false, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
+  if (tiles_128x128 >= sms / 2)
+    return launch_cfg<false, 1, 128>(weight, scales, bias, input, output, m, n, k, stream);
+  return launch_cfg<false, 1, 64>(weight, scales, bias, input, output, m, n, k, stream);
+}
+
+}  // namespace b200

@@ -1,0 +1,542 @@
+// Decode GEMV (M = 1) and fused LM-head GEMV + argmax for sm_100a.
+//
+// Replaces the reference's gemv_bf16 / gemv_w8a16 / lm_head_bf16 /
+// argmax_bf16 (reference src/cuda/kernels.cu:326-603, 953-1041, 1540-1655).
+//
+// Design (B200): the GEMV is a pure HBM stream of the weight matrix, so the
+// kernel is organised around bytes in flight rather than around rows:
+//  * a "team" of TPR threads owns R consecutive rows; each thread walks the
+//    row in 16-byte chunks (c = t, t+TPR, ...), loading the same chunk of all
+//    R rows, so one shared-memory read of x feeds R rows;
+//  * U chunk-columns are loaded before any arithmetic (R*U 128-bit loads in
+//    flight per thread, non-allocating in L1);
+//  * INT8 -> FP32 uses the exact magic-number conversion (two ALU ops per
+//    byte, no I2F), the 16 products of a chunk are summed in FP32 and the
+//    chunk sum is multiplied by the BF16 group scale once (a chunk never
+//    straddles a 64-wide group);
+//  * TPR / R are picked per shape so that small matrices spread over every
+//    SM and large ones keep each thread busy (choose_config);
+//  * launches carry the programmatic-dependent-launch attribute: the weight
+//    prefetch is issued before griddepcontrol.wait, so a chain of Linear
+//    calls overlaps one kernel's tail with the next one's weight stream.
+//    Nothing is written to global memory before the wait.
+//
+// The LM-head form adds a per-CTA argmax over the BF16-rounded logits
+// (lowest index on ties) written to the caller's workspace, and a one-CTA
+// reduction kernel (launched with PDL) that writes the final index.
+
+#include <cfloat>
+#include <climits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace b200 {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile(
+      "ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+
+// acc += sum_{j<4} q_j * x_j for the four int8 of one packed word.
+__device__ __forceinline__ float dot4_s8(uint32_t packed, const float* x,
+                                         float acc) {
+  const uint32_t b = packed ^ 0x80808080u;
+  acc = fmaf(s8_to_f32_biased<0>(b), x[0], acc);
+  acc = fmaf(s8_to_f32_biased<1>(b), x[1], acc);
+  acc = fmaf(s8_to_f32_biased<2>(b), x[2], acc);
+  acc = fmaf(s8_to_f32_biased<3>(b), x[3], acc);
+  return acc;
+}
+
+__device__ __forceinline__ float dot2_bf16(uint32_t w, float x0, float x1,
+                                           float acc) {
+  acc = fmaf(bf16_lo(w), x0, acc);
+  acc = fmaf(bf16_hi(w), x1, acc);
+  return acc;
+}
+
+// Strictly-greater update with lowest index on ties; values <= -FLT_MAX
+// never win (reference argmax semantics, src/cuda/kernels.cu:326-356).
+__device__ __forceinline__ void argmax_update(float& best, int& best_index,
+                                              float v, int index) {
+  if (v > best || (v == best && v > -FLT_MAX && index < best_index)) {
+    best = v;
+    best_index = index;
+  }
+}
+
+template <bool kW8, int kTPR, int kR>
+__global__ void __launch_bounds__(kThreads, 2)
+gemv_stream_kernel(const void* __restrict__ weight,
+                   const bf16* __restrict__ scales,
+                   const bf16* __restrict__ bias,
+                   const bf16* __restrict__ input, bf16* __restrict__ output,
+                   int n_rows, int k, float* __restrict__ block_value,
+                   int* __restrict__ block_index) {
+  constexpr int kTeams = kThreads / kTPR;
+  constexpr int kU = kR == 1 ? 4 : 2;  // chunk columns in flight per thread
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem_raw);  // k bf16 (pairs)
+  __shared__ float red_val[kThreads / 32 > 0 ? kThreads / 32 : 1][kR];
+  __shared__ float team_best[kTeams];
+  __shared__ int team_best_index[kTeams];
+
+  const int team = threadIdx.x / kTPR;
+  const int t = threadIdx.x % kTPR;
+  const int row0 = (blockIdx.x * kTeams + team) * kR;
+  const int chunks = kW8 ? (k >> 4) : (k >> 3);
+  const int groups = (k + 63) >> 6;
+  const size_t row_bytes = kW8 ? size_t(k) : size_t(k) * 2;
+  const unsigned char* wbase = static_cast<const unsigned char*>(weight);
+
+  bool valid[kR];
+  const unsigned char* wrow[kR];
+#pragma unroll
+  for (int r = 0; r < kR; ++r) {
+    valid[r] = row0 + r < n_rows;
+    wrow[r] = wbase + size_t(valid[r] ? row0 + r : 0) * row_bytes;
+  }
+
+  // First batch of weight loads does not depend on the previous kernel.
+  uint4 w[kU][kR];
+  int base = t;
+#pragma unroll
+  for (int u = 0; u < kU; ++u) {
+    const int c = base + u * kTPR;
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      w[u][r] = (c < chunks && valid[r]) ? ld_stream16(wrow[r] + size_t(c) * 16)
+                                         : make_uint4(0, 0, 0, 0);
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait_primary();
+
+  // Stage x (BF16) in shared memory with 16-byte copies.
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(input);
+    uint4* dst = reinterpret_cast<uint4*>(xs);
+    for (int i = threadIdx.x; i < (k >> 3); i += kThreads) dst[i] = src[i];
+  }
+  __syncthreads();
+
+  float acc[kR];
+#pragma unroll
+  for (int r = 0; r < kR; ++r) acc[r] = 0.0f;
+
+  while (true) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c = base + u * kTPR;
+      if (c < chunks) {
+        if constexpr (kW8) {
+          const uint4 xa = reinterpret_cast<const uint4*>(xs)[2 * c];
+          const uint4 xb = reinterpret_cast<const uint4*>(xs)[2 * c + 1];
+          float xf[16];
+          xf[0] = bf16_lo(xa.x); xf[1] = bf16_hi(xa.x);
+          xf[2] = bf16_lo(xa.y); xf[3] = bf16_hi(xa.y);
+          xf[4] = bf16_lo(xa.z); xf[5] = bf16_hi(xa.z);
+          xf[6] = bf16_lo(xa.w); xf[7] = bf16_hi(xa.w);
+          xf[8] = bf16_lo(xb.x); xf[9] = bf16_hi(xb.x);
+          xf[10] = bf16_lo(xb.y); xf[11] = bf16_hi(xb.y);
+          xf[12] = bf16_lo(xb.z); xf[13] = bf16_hi(xb.z);
+          xf[14] = bf16_lo(xb.w); xf[15] = bf16_hi(xb.w);
+#pragma unroll
+          for (int r = 0; r < kR; ++r) {
+            float p = 0.0f;
+            p = dot4_s8(w[u][r].x, xf + 0, p);
+            p = dot4_s8(w[u][r].y, xf + 4, p);
+            p = dot4_s8(w[u][r].z, xf + 8, p);
+            p = dot4_s8(w[u][r].w, xf + 12, p);
+            const float s =
+                valid[r] ? __bfloat162float(
+                               scales[size_t(row0 + r) * groups + (c >> 2)])
+                         : 0.0f;
+            acc[r] = fmaf(p, s, acc[r]);
+          }
+        } else {
+          const uint4 xa = reinterpret_cast<const uint4*>(xs)[c];
+          const float x0 = bf16_lo(xa.x), x1 = bf16_hi(xa.x);
+          const float x2 = bf16_lo(xa.y), x3 = bf16_hi(xa.y);
+          const float x4 = bf16_lo(xa.z), x5 = bf16_hi(xa.z);
+          const float x6 = bf16_lo(xa.w), x7 = bf16_hi(xa.w);
+#pragma unroll
+          for (int r = 0; r < kR; ++r) {
+            float a = acc[r];
+            a = dot2_bf16(w[u][r].x, x0, x1, a);
+            a = dot2_bf16(w[u][r].y, x2, x3, a);
+            a = dot2_bf16(w[u][r].z, x4, x5, a);
+            a = dot2_bf16(w[u][r].w, x6, x7, a);
+            acc[r] = a;
+          }
+        }
+      }
+    }
+    base += kU * kTPR;
+    if (base >= chunks) break;
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c = base + u * kTPR;
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        w[u][r] = (c < chunks && valid[r])
+                      ? ld_stream16(wrow[r] + size_t(c) * 16)
+                      : make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  // Team reduction.
+  constexpr int kWarpSpan = kTPR < 32 ? kTPR : 32;
+#pragma unroll
+  for (int r = 0; r < kR; ++r) {
+#pragma unroll
+    for (int off = kWarpSpan / 2; off > 0; off >>= 1) {
+      acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+    }
+  }
+  if constexpr (kTPR > 32) {
+    constexpr int kWarpsPerTeam = kTPR / 32;
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+      for (int r = 0; r < kR; ++r) red_val[warp][r] = acc[r];
+    }
+    __syncthreads();
+    if (t == 0) {
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kWarpsPerTeam; ++i) s += red_val[warp + i][r];
+        acc[r] = s;
+      }
+    }
+  }
+
+  if (t == 0) {
+    float best = -FLT_MAX;
+    int best_index = INT_MAX;
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      if (valid[r]) {
+        const float b = bias ? __bfloat162float(bias[row0 + r]) : 0.0f;
+        const bf16 y = __float2bfloat16_rn(acc[r] + b);
+        output[row0 + r] = y;
+        argmax_update(best, best_index, __bfloat162float(y), row0 + r);
+      }
+    }
+    if (block_value != nullptr) {
+      team_best[team] = best;
+      team_best_index[team] = best_index;
+    }
+  }
+  if (block_value != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float best = -FLT_MAX;
+      int best_index = INT_MAX;
+      for (int i = 0; i < kTeams; ++i) {
+        argmax_update(best, best_index, team_best[i], team_best_index[i]);
+      }
+      block_value[blockIdx.x] = best;
+      block_index[blockIdx.x] = best_index;
+    }
+  }
+}
+
+// Any alignment / any K: one warp per row, scalar loads.  Also the LM-head
+// form with 8 rows per CTA, so ceil(vocab/8) CTAs match the reference's
+// workspace sizing (src/qwen2.cpp:193-198).
+template <bool kW8>
+__global__ void __launch_bounds__(kThreads)
+gemv_generic_kernel(const void* __restrict__ weight,
+                    const bf16* __restrict__ scales,
+                    const bf16* __restrict__ bias,
+                    const bf16* __restrict__ input, bf16* __restrict__ output,
+                    int n_rows, int k, float* __restrict__ block_value,
+                    int* __restrict__ block_index) {
+  __shared__ float row_val[kThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kThreads / 32) + warp;
+  const int groups = (k + 63) >> 6;
+  float acc = 0.0f;
+  if (row < n_rows) {
+    if constexpr (kW8) {
+      const int8_t* w = static_cast<const int8_t*>(weight) + size_t(row) * k;
+      const bf16* s = scales + size_t(row) * groups;
+      for (int i = lane; i < k; i += 32) {
+        acc = fmaf(float(w[i]) * __bfloat162float(s[i >> 6]),
+                   __bfloat162float(input[i]), acc);
+      }
+    } else {
+      const bf16* w = static_cast<const bf16*>(weight) + size_t(row) * k;
+      for (int i = lane; i < k; i += 32) {
+        acc = fmaf(__bfloat162float(w[i]), __bfloat162float(input[i]), acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  }
+  if (lane == 0) {
+    float v = -FLT_MAX;
+    if (row < n_rows) {
+      const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
+      const bf16 y = __float2bfloat16_rn(acc + b);
+      output[row] = y;
+      v = __bfloat162float(y);
+    }
+    row_val[warp] = v;
+  }
+  if (block_value != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float best = -FLT_MAX;
+      int best_index = INT_MAX;
+      for (int i = 0; i < kThreads / 32; ++i) {
+        const int r = blockIdx.x * (kThreads / 32) + i;
+        if (r < n_rows) argmax_update(best, best_index, row_val[i], r);
+      }
+      block_value[blockIdx.x] = best;
+      block_index[blockIdx.x] = best_index;
+    }
+  }
+}
+
+// Final argmax over per-CTA (value, index) pairs; one CTA.
+__global__ void __launch_bounds__(1024)
+argmax_partials_kernel(const float* __restrict__ block_value,
+                       const int* __restrict__ block_index, int count,
+                       int* __restrict__ argmax) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait_primary();
+  float best = -FLT_MAX;
+  int best_index = INT_MAX;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    argmax_update(best, best_index, block_value[i], block_index[i]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_index, off);
+    argmax_update(best, best_index, ov, oi);
+  }
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[warp] = best;
+    si[warp] = best_index;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int i = 0; i < int(blockDim.x >> 5); ++i) argmax_update(b, bi, sv[i], si[i]);
+    *argmax = bi == INT_MAX ? 0 : bi;
+  }
+}
+
+// Argmax over BF16 values, one CTA (n is a vocabulary, not a matrix).
+__global__ void __launch_bounds__(1024)
+argmax_bf16_kernel(const bf16* __restrict__ values, int n,
+                   int* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait_primary();
+  float best = -FLT_MAX;
+  int best_index = INT_MAX;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    argmax_update(best, best_index, __bfloat162float(values[i]), i);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_index, off);
+    argmax_update(best, best_index, ov, oi);
+  }
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[warp] = best;
+    si[warp] = best_index;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int i = 0; i < int(blockDim.x >> 5); ++i) argmax_update(b, bi, sv[i], si[i]);
+    *out = bi == INT_MAX ? 0 : bi;
+  }
+}
+
+struct GemvConfig {
+  int tpr;  // threads per team
+  int r;    // rows per team
+};
+
+// Shape heuristic: large matrices (more 16-byte chunks than ~8 per thread of
+// a full B200) use 4 rows per team to amortise x; everything else spreads the
+// matrix over as many threads as possible, <= 2 chunk columns per thread.
+GemvConfig choose_config(int n_rows, int chunks, bool lm_head) {
+  const long long total = (long long)n_rows * chunks;
+  const bool big = total >= 148LL * 2048 * 4;
+  const int r = big ? 4 : 1;
+  const int per_thread = big ? 8 : 2;
+  int want = (chunks + per_thread - 1) / per_thread;
+  int tpr = 4;
+  while (tpr < want && tpr < 256) tpr <<= 1;
+  if (lm_head && tpr > 32) tpr = 32;
+  return {tpr, r};
+}
+
+template <bool kW8, int kTPR, int kR>
+cudaError_t launch_stream(const void* w, const bf16* s, const bf16* b,
+                          const bf16* x, bf16* y, int n, int k, float* bv,
+                          int* bi, cudaStream_t stream, int* grid_out) {
+  constexpr int kRowsPerBlock = (kThreads / kTPR) * kR;
+  const int grid = (n + kRowsPerBlock - 1) / kRowsPerBlock;
+  const size_t smem = size_t(k) * 2;
+  auto kernel = gemv_stream_kernel<kW8, kTPR, kR>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (grid_out) *grid_out = grid;
+  return cudaLaunchKernelEx(&cfg, kernel, w, s, b, x, y, n, k, bv, bi);
+}
+
+template <bool kW8, int kR>
+cudaError_t dispatch_tpr(int tpr, const void* w, const bf16* s, const bf16* b,
+                         const bf16* x, bf16* y, int n, int k, float* bv,
+                         int* bi, cudaStream_t st, int* grid) {
+  switch (tpr) {
+    case 4: return launch_stream<kW8, 4, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+    case 8: return launch_stream<kW8, 8, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+    case 16: return launch_stream<kW8, 16, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+    case 32: return launch_stream<kW8, 32, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+    case 64: return launch_stream<kW8, 64, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+    case 128: return launch_stream<kW8, 128, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+    default: return launch_stream<kW8, 256, kR>(w, s, b, x, y, n, k, bv, bi, st, grid);
+  }
+}
+
+template <bool kW8>
+cudaError_t launch_generic(const void* w, const bf16* s, const bf16* b,
+                           const bf16* x, bf16* y, int n, int k, float* bv,
+                           int* bi, cudaStream_t stream, int* grid_out) {
+  const int grid = (n + 7) / 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (grid_out) *grid_out = grid;
+  return cudaLaunchKernelEx(&cfg, gemv_generic_kernel<kW8>, w, s, b, x, y, n,
+                            k, bv, bi);
+}
+
+bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace
+
+bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
+                         int k) {
+  const int elems_per_chunk = w8 ? 16 : 8;
+  return k > 0 && k % elems_per_chunk == 0 && k <= 98304 &&
+         aligned16(weight) && aligned16(input);
+}
+
+cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
+                        const bf16* bias, const bf16* input, bf16* output,
+                        int n, int k, float* block_value, int* block_index,
+                        cudaStream_t stream, int* grid_out) {
+  if (n <= 0) {
+    if (grid_out) *grid_out = 0;
+    return cudaSuccess;
+  }
+  if (!gemv_uses_fast_path(w8, weight, input, k)) {
+    return w8 ? launch_generic<true>(weight, scales, bias, input, output, n, k,
+                                     block_value, block_index, stream, grid_out)
+              : launch_generic<false>(weight, scales, bias, input, output, n,
+                                      k, block_value, block_index, stream,
+                                      grid_out);
+  }
+  const int chunks = w8 ? k / 16 : k / 8;
+  const GemvConfig c = choose_config(n, chunks, block_value != nullptr);
+  if (w8) {
+    return c.r == 4 ? dispatch_tpr<true, 4>(c.tpr, weight, scales, bias, input,
+                                            output, n, k, block_value,
+                                            block_index, stream, grid_out)
+                    : dispatch_tpr<true, 1>(c.tpr, weight, scales, bias, input,
+                                            output, n, k, block_value,
+                                            block_index, stream, grid_out);
+  }
+  return c.r == 4 ? dispatch_tpr<false, 4>(c.tpr, weight, scales, bias, input,
+                                           output, n, k, block_value,
+                                           block_index, stream, grid_out)
+                  : dispatch_tpr<false, 1>(c.tpr, weight, scales, bias, input,
+                                           output, n, k, block_value,
+                                           block_index, stream, grid_out);
+}
+
+cudaError_t launch_argmax_partials(const float* block_value,
+                                   const int* block_index, int count,
+                                   int* argmax, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, argmax_partials_kernel, block_value,
+                            block_index, count, argmax);
+}
+
+cudaError_t launch_argmax_bf16(const bf16* values, int n, int* out,
+                               cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, argmax_bf16_kernel, values, n, out);
+}
+
+}  // namespace b200

@@ -1,0 +1,38 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+using bf16 = __nv_bfloat16;
+
+// gemv.cu
+bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
+                         int k);
+// Launches the GEMV (block_value == nullptr) or the LM-head GEMV with
+// per-CTA argmax partials; *grid_out receives the CTA count.
+cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
+                        const bf16* bias, const bf16* input, bf16* output,
+                        int n, int k, float* block_value, int* block_index,
+                        cudaStream_t stream, int* grid_out);
+cudaError_t launch_argmax_partials(const float* block_value,
+                                   const int* block_index, int count,
+                                   int* argmax, cudaStream_t stream);
+cudaError_t launch_argmax_bf16(const bf16* values, int n, int* out,
+                               cudaStream_t stream);
+
+// gemm_simt.cu: any shape / alignment, CUDA cores.
+cudaError_t launch_gemm_simt(bool w8, const void* weight, const bf16* scales,
+                             const bf16* bias, const bf16* input, bf16* output,
+                             int m, int n, int k, cudaStream_t stream);
+
+// gemm_sm100.cu: tcgen05 + TMA + TMEM path.
+bool gemm_tc_supported(bool w8, const void* weight, const void* input,
+                       const void* output, int m, int n, int k);
+cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
+                           const bf16* bias, const bf16* input, bf16* output,
+                           int m, int n, int k, cudaStream_t stream);
+
+}  // namespace b200

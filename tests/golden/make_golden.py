@@ -1,0 +1,96 @@
+"""Generates the CPU golden fixtures in this directory from the REFERENCE itself.
+
+Run in a container that has the reference checkout (default /root/reference,
+override with --reference) and the reference CPU Linear built into
+oracle/_ref (``make -C oracle ref``):
+
+    python tests/golden/make_golden.py
+
+Outputs (committed, small):
+  exporter_kat.npz   reference tools/export_model.py float32_to_bfloat16 and
+                     quantize_groupwise on seeded inputs (group 64, a K=70
+                     tail, an all-zero group), i.e. the W8A16 qbin format;
+  cpu_linear.npz     reference src/cpu_ops.cpp linear_fp32 / linear_fp32_batch
+                     (OpenBLAS FP32) on the deterministic BF16 patterns of the
+                     reference's tests/test_cuda.cpp:621-703 (check_bf16_linear_case).
+The tests compare the oracle (oracle/linear_oracle.c) against these.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+
+def bf16_linear_patterns(tokens, out_features, in_features):
+    """Input patterns of reference tests/test_cuda.cpp:621-637."""
+    idx_w = np.arange(out_features * in_features)
+    weight = ((idx_w % 17) - 8).astype(np.float32) * 0.015625
+    idx_x = np.arange(tokens * in_features)
+    x = ((idx_x % 13) - 6).astype(np.float32) * 0.03125
+    bias = ((np.arange(out_features) % 5) - 2).astype(np.float32) * 0.0625
+    return (weight.reshape(out_features, in_features),
+            x.reshape(tokens, in_features), bias)
+
+
+BF16_CASES = [(3, 11, 14, True), (2, 5, 7, True), (3, 23, 14, False),
+              (32, 64, 64, True), (31, 37, 33, True), (65, 70, 67, False)]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.join(args.reference, "tools"))
+    import export_model as E  # the reference exporter
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(20240611)
+    # --- BF16 conversion known answers (exporter self-test values + random).
+    special = np.array([0.0, -0.0, 1.0, -2.5, np.inf, -np.inf, np.nan,
+                        1.0 + 1.0 / 256.0,
+                        np.nextafter(np.float32(1.0 + 1.0 / 256.0), np.float32(np.inf)),
+                        3.0e38, -1.0e-40, 65504.0, 1.0 / 3.0], dtype=np.float32)
+    randv = (rng.standard_normal(4096) * np.exp(rng.uniform(-20, 20, 4096))).astype(np.float32)
+    f32 = np.concatenate([special, randv])
+    bf16_bits = E.float32_to_bfloat16(f32)
+
+    # --- Quantiser: seeded N(0, 0.02) weights, group 64, tails and a zero group.
+    quant = {}
+    for name, (rows, cols) in {"q_24x200": (24, 200), "q_8x70": (8, 70),
+                               "q_16x896": (16, 896), "q_5x65": (5, 65)}.items():
+        w = rng.normal(0.0, 0.02, (rows, cols)).astype(np.float32)
+        w[rows - 1, :min(64, cols)] = 0.0      # an all-zero group -> scale 1.0
+        w[0, 0] = 0.04                          # a row whose max is a round value
+        q, s, _, _ = E.quantize_groupwise(w, 64)
+        quant[name + "_w"] = w
+        quant[name + "_q"] = q
+        quant[name + "_s"] = E.float32_to_bfloat16(s).reshape(s.shape)
+    np.savez_compressed(os.path.join(HERE, "exporter_kat.npz"),
+                        f32=f32, bf16_bits=bf16_bits, **quant)
+
+    # --- Reference CPU FP32 Linear on the reference test patterns.
+    if O.ref_cpu() is None:
+        raise SystemExit("oracle/_ref/libref_cpu_linear.so missing: make -C oracle ref")
+    out = {}
+    for (m, n, k, with_bias) in BF16_CASES:
+        w, x, b = bf16_linear_patterns(m, n, k)
+        wb, xb, bb = (O.bf16_to_f32(E.float32_to_bfloat16(a)).reshape(a.shape)
+                      for a in (w, x, b))
+        y = O.ref_cpu_linear(wb, bb if with_bias else None, xb)
+        y1 = O.ref_cpu_linear(wb, bb if with_bias else None, xb[0])
+        tag = f"{m}x{n}x{k}"
+        out[tag + "_batch"] = y
+        out[tag + "_gemv"] = y1
+    np.savez_compressed(os.path.join(HERE, "cpu_linear.npz"), **out)
+    print("wrote exporter_kat.npz, cpu_linear.npz")
+
+
+if __name__ == "__main__":
+    main()

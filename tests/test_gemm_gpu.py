@@ -1,0 +1,153 @@
+"""Prefill GEMM (tcgen05 tensor-core path and CUDA-core fallback) on the GPU
+against the oracle: the reference test shapes (tests/test_cuda.cpp:694-703,
+882-919) and the BASELINE prefill sweep on sampled rows."""
+import numpy as np
+import pytest
+
+from conftest import from_bits, to_bits
+from patterns import PREFILL_M, QWEN_SHAPES, seeded_linear, w8a16_case
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16_tol(e):
+    return np.maximum(0.004, np.abs(e) * 0.008)
+
+
+def w8_tol(e):
+    return np.maximum(1.0 / 64, np.abs(e) * 0.01)
+
+
+def north_star_ok(a, e):
+    return np.all(np.abs(a - e) <= 2e-2 + 1e-2 * np.abs(e))
+
+
+def bf16_linear_patterns(tokens, n, k):
+    from golden.make_golden import bf16_linear_patterns as p
+    return p(tokens, n, k)
+
+
+@pytest.mark.parametrize("m,n,k,with_bias",
+                         [(3, 11, 14, True), (2, 5, 7, True), (3, 23, 14, False),
+                          (32, 64, 64, True), (31, 37, 33, True), (65, 70, 67, False),
+                          (130, 200, 136, True), (257, 384, 512, False)])
+def test_gemm_bf16_reference_shapes(b200, oracle, cuda, m, n, k, with_bias):
+    import torch
+    w, x, b = bf16_linear_patterns(m, n, k)
+    wb, xb, bb = oracle.f32_to_bf16(w), oracle.f32_to_bf16(x), oracle.f32_to_bf16(b)
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    b200.gemm_bf16(from_bits(wb, cuda), from_bits(bb, cuda) if with_bias else None,
+                   from_bits(xb, cuda), y, m, n, k)
+    got = oracle.bf16_to_f32(to_bits(y))
+    exp = oracle.linear_bf16(wb, bb if with_bias else None, xb)
+    assert np.all(np.abs(got - exp) <= bf16_tol(exp))
+
+
+W8_CASES = ([(3, 5, 70, True), (2, 7, 65, False)] +
+            [(2, n, k, bias) for (n, k, bias) in [(896, 896, True), (128, 896, True),
+                                                   (4864, 896, False), (896, 4864, False)]] +
+            [(t, n, k, bias) for t in (32, 128, 512)
+             for (n, k, bias) in [(896, 896, True), (4864, 896, False), (896, 4864, False)]] +
+            [(200, 96, 912, False), (129, 24, 1024, True)])
+
+
+@pytest.mark.parametrize("m,n,k,with_bias", W8_CASES)
+def test_gemm_w8a16_reference_shapes(b200, oracle, cuda, m, n, k, with_bias):
+    """reference check_w8a16_linear_case: GEMM vs the dequantised reference
+    and GEMV row 0 vs GEMM row 0."""
+    import torch
+    q, s, x, b = w8a16_case(m, n, k)
+    sb, xb, bb = oracle.f32_to_bf16(s), oracle.f32_to_bf16(x), oracle.f32_to_bf16(b)
+    dq, ds, dx = torch.from_numpy(q).to(cuda), from_bits(sb, cuda), from_bits(xb, cuda)
+    db = from_bits(bb, cuda) if with_bias else None
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    b200.gemm_w8a16(dq, ds, 64, db, dx, y, m, n, k)
+    got = oracle.bf16_to_f32(to_bits(y))
+    exp = oracle.bf16_to_f32(oracle.linear_w8a16(q, sb, bb if with_bias else None, xb,
+                                                 gemm=True))
+    assert np.all(np.abs(got - exp) <= w8_tol(exp))
+    gv = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+    b200.gemv_w8a16(dq, ds, 64, db, dx[0], gv, n, k)
+    gvf = oracle.bf16_to_f32(to_bits(gv))
+    assert np.all(np.abs(gvf - got[0]) <= w8_tol(got[0]))
+
+
+@pytest.mark.parametrize("m", PREFILL_M)
+@pytest.mark.parametrize("k,n", QWEN_SHAPES)
+@pytest.mark.parametrize("w8", [True, False])
+def test_gemm_prefill_sweep_sampled_rows(b200, oracle, cuda, m, k, n, w8):
+    """configs[2] sizes; the oracle checks 24 sampled rows (all rows at M=32)."""
+    import torch
+    if m * n > 8192 * 4864 and not w8:
+        m = 2048  # keep the BF16 896->151936 case at a size the oracle samples quickly
+    w, bias = seeded_linear(n, k, seed=77 + k + n, bias=(n <= 896))
+    rng = np.random.default_rng(m + k + n)
+    x = oracle.f32_to_bf16(rng.standard_normal((m, k)).astype(np.float32))
+    bb = oracle.f32_to_bf16(bias) if bias is not None else None
+    db = from_bits(bb, cuda) if bb is not None else None
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    rows = np.arange(m) if m <= 32 else np.unique(np.concatenate(
+        [[0, m - 1], rng.choice(m, 22, replace=False)]))
+    if w8:
+        q, sb = oracle.quantize_groupwise(w)
+        b200.gemm_w8a16(torch.from_numpy(q).to(cuda), from_bits(sb, cuda), 64, db,
+                        from_bits(x, cuda), y, m, n, k)
+        exp = oracle.bf16_to_f32(oracle.linear_w8a16(q, sb, bb, x[rows], gemm=True))
+    else:
+        wb = oracle.f32_to_bf16(w)
+        b200.gemm_bf16(from_bits(wb, cuda), db, from_bits(x, cuda), y, m, n, k)
+        exp = oracle.bf16_to_f32(oracle.f32_to_bf16(oracle.linear_bf16(wb, bb, x[rows])))
+    ybits = to_bits(y)
+    got = oracle.bf16_to_f32(ybits[rows])
+    assert north_star_ok(got, exp)
+    assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
+    assert np.isfinite(oracle.bf16_to_f32(ybits)).all()
+
+
+def test_gemm_matches_reference_cuda_kernels(b200, oracle, cuda):
+    import torch
+    ref = oracle.ref_cuda()
+    if ref is None:
+        pytest.skip("oracle/_ref/libref_kernels.so not built")
+    s = torch.cuda.current_stream().cuda_stream
+    for (m, k, n) in [(128, 896, 896), (512, 896, 4864), (128, 4864, 896)]:
+        w, _ = seeded_linear(n, k, seed=m + n)
+        q, sb = oracle.quantize_groupwise(w)
+        x = oracle.f32_to_bf16(np.random.default_rng(m).standard_normal((m, k)).astype(np.float32))
+        dq, ds, dx = torch.from_numpy(q).to(cuda), from_bits(sb, cuda), from_bits(x, cuda)
+        ours = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+        theirs = torch.empty_like(ours)
+        b200.gemm_w8a16(dq, ds, 64, None, dx, ours, m, n, k)
+        assert ref.ref_gemm_w8a16(dq.data_ptr(), ds.data_ptr(), 64, None, dx.data_ptr(),
+                                  theirs.data_ptr(), m, n, k, s) == 0
+        a, r = oracle.bf16_to_f32(to_bits(ours)), oracle.bf16_to_f32(to_bits(theirs))
+        assert north_star_ok(a, r)
+        assert np.all(np.abs(a - r) <= w8_tol(r))
+        wb = oracle.f32_to_bf16(w)
+        dw = from_bits(wb, cuda)
+        b200.gemm_bf16(dw, None, dx, ours, m, n, k)
+        assert ref.ref_gemm_bf16(dw.data_ptr(), None, dx.data_ptr(), theirs.data_ptr(),
+                                 m, n, k, s) == 0
+        a, r = oracle.bf16_to_f32(to_bits(ours)), oracle.bf16_to_f32(to_bits(theirs))
+        assert np.all(np.abs(a - r) <= bf16_tol(r))
+
+
+def test_gemm_output_guard_band_and_status(b200, oracle, cuda):
+    """Nothing is written outside Y (guard bands), tails in M and N."""
+    import torch
+    m, n, k = 133, 200, 192
+    w, _ = seeded_linear(n, k, seed=5)
+    q, sb = oracle.quantize_groupwise(w)
+    x = oracle.f32_to_bf16(np.random.default_rng(1).standard_normal((m, k)).astype(np.float32))
+    guard = 4096
+    buf = torch.full((m * n + 2 * guard,), 7.0, dtype=torch.bfloat16, device=cuda)
+    y = buf[guard:guard + m * n].view(m, n)
+    b200.gemm_w8a16(torch.from_numpy(q).to(cuda), from_bits(sb, cuda), 64, None,
+                    from_bits(x, cuda), y, m, n, k)
+    head, tail = to_bits(buf[:guard]), to_bits(buf[guard + m * n:])
+    seven = oracle.f32_to_bf16(np.array([7.0], np.float32))[0]
+    assert (head == seven).all() and (tail == seven).all()
+    exp = oracle.bf16_to_f32(oracle.linear_w8a16(q, sb, None, x, gemm=True))
+    got = oracle.bf16_to_f32(to_bits(y))
+    assert np.all(np.abs(got - exp) <= w8_tol(exp))
+    assert b200.device_status() == 0
