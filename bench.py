@@ -357,6 +357,38 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_case(args):
+    """One kernel, `warmup` + `steps` launches, for ncu captures (no timing)."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    b200 = load_pkg()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    m, n, k = args.m, args.n, args.k
+    w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+    q, s = b200.quantize_groupwise(w)
+    wb = w.to(torch.bfloat16)
+    del w
+    x = torch.randn(m if args.case.startswith("gemm") else 1, k, generator=gen,
+                    device=dev).to(torch.bfloat16)
+    y = torch.empty(x.shape[0], n, dtype=torch.bfloat16, device=dev)
+    bv, bi = b200.lm_head_workspace(n, dev)
+    am = torch.empty(1, dtype=torch.int32, device=dev)
+    calls = {
+        "gemv_w8": lambda: b200.gemv_w8a16(q, s, 64, None, x, y, n, k),
+        "gemv_bf16": lambda: b200.gemv_bf16(wb, None, x, y, n, k),
+        "lm_head": lambda: b200.lm_head_bf16(wb, None, x, y, bv, bi, am, n, k),
+        "gemm_w8": lambda: b200.gemm_w8a16(q, s, 64, None, x, y, m, n, k),
+        "gemm_bf16": lambda: b200.gemm_bf16(wb, None, x, y, m, n, k),
+    }
+    fn = calls[args.case]
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "m": m, "n": n, "k": k,
+                      "launches": args.warmup + args.steps}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -366,9 +398,17 @@ def main():
     ap.add_argument("--passes", type=int, default=100, help="sweep passes per step")
     ap.add_argument("--no-gemm", action="store_true", help="skip the GEMM sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--case", default=None,
+                    help="profiling mode: run only one kernel, `--steps` launches "
+                         "(gemv_w8, gemv_bf16, lm_head, gemm_w8, gemm_bf16)")
+    ap.add_argument("--m", type=int, default=2048)
+    ap.add_argument("--n", type=int, default=151936)
+    ap.add_argument("--k", type=int, default=896)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.case:
+        return run_case(args)
 
     world, rank, local = init_dist()
     device = torch.device("cuda", local)

@@ -8,6 +8,7 @@
 
 namespace b200 {
 cudaError_t read_device_status(int* value, bool clear);  // gemm_sm100.cu
+cudaError_t read_gemv_status(int* value, bool clear);    // gemv.cu
 }
 
 using b200::bf16;
@@ -119,10 +120,11 @@ const char* b200_status_string(int status) {
 }
 
 int b200_device_status(int clear) {
-  int value = 0;
-  cudaError_t e = b200::read_device_status(&value, clear != 0);
+  int gemm = 0, gemv = 0;
+  cudaError_t e = b200::read_device_status(&gemm, clear != 0);  // synchronises
+  if (e == cudaSuccess) e = b200::read_gemv_status(&gemv, clear != 0);
   if (e != cudaSuccess) return -int(e);
-  return value;
+  return gemm != 0 ? gemm : gemv;
 }
 
 int b200_gemv_bf16(const uint16_t* weight, const uint16_t* bias,

@@ -382,6 +382,285 @@ argmax_bf16_kernel(const bf16* __restrict__ values, int n,
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Main decode path: weight tiles streamed by the TMA engine.
+//
+// One persistent CTA per SM.  Warp 0 (one lane) is the producer: for each
+// tile of kTileRows consecutive rows -- a contiguous byte range of W, plus
+// the matching contiguous range of the W8 scales -- it issues 1-D bulk
+// copies (cp.async.bulk) into a ring of shared-memory stages guarded by
+// full/empty mbarriers.  Because the weights never depend on the previous
+// kernel, the producer starts before griddepcontrol.wait and the ring
+// keeps ~100-200 KB per SM in flight regardless of how long the arithmetic
+// takes.  Warps 1..8 are consumers: warp w owns kR rows of every tile; lane
+// l handles 16-byte chunks c = l, l+32, ... of those rows, reading x from a
+// shared FP32 copy laid out as kEPC/4 "planes" (plane p holds elements
+// 4p..4p+3 of every chunk) so that consecutive lanes read consecutive
+// 16-byte words (no bank conflicts).  The INT8 products use the sm_100
+// packed FP32 instructions (2 elements per FADD2 / FFMA2).
+constexpr int kConsumerWarps = 8;
+constexpr int kBulkThreads = 32 * (kConsumerWarps + 1);
+constexpr int kBulkSmemBudget = 200 * 1024;
+constexpr int kMaxStages = 6;
+
+static __device__ int g_gemv_status = 0;
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+// Packed: a += q(4 int8 of `packed`) * x[0..3].
+__device__ __forceinline__ float2 dot4_s8_x2(uint32_t packed, float4 x,
+                                             float2 a) {
+  const uint32_t b = packed ^ 0x80808080u;
+  const float2 bias = f2(-8388736.0f, -8388736.0f);
+  const float2 q01 = __fadd2_rn(
+      f2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7540u)),
+         __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7541u))),
+      bias);
+  const float2 q23 = __fadd2_rn(
+      f2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7542u)),
+         __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7543u))),
+      bias);
+  a = __ffma2_rn(q01, f2(x.x, x.y), a);
+  a = __ffma2_rn(q23, f2(x.z, x.w), a);
+  return a;
+}
+
+__device__ __forceinline__ float2 dot4_bf16_x2(uint32_t w01, uint32_t w23,
+                                               float4 x, float2 a) {
+  a = __ffma2_rn(f2(bf16_lo(w01), bf16_hi(w01)), f2(x.x, x.y), a);
+  a = __ffma2_rn(f2(bf16_lo(w23), bf16_hi(w23)), f2(x.z, x.w), a);
+  return a;
+}
+
+template <bool kW8, int kR>
+__global__ void __launch_bounds__(kBulkThreads, 1)
+gemv_bulk_kernel(const void* __restrict__ weight,
+                 const bf16* __restrict__ scales,
+                 const bf16* __restrict__ bias,
+                 const bf16* __restrict__ input, bf16* __restrict__ output,
+                 int n_rows, int k, int stages, int stage_bytes,
+                 int w_tile_bytes, float* __restrict__ block_value,
+                 int* __restrict__ block_index) {
+  constexpr int kEPC = kW8 ? 16 : 8;  // elements per 16-byte chunk
+  constexpr int kPlanes = kEPC / 4;
+  constexpr int kTileRows = kConsumerWarps * kR;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row_bytes = kW8 ? k : 2 * k;
+  const int chunks = k / kEPC;
+  const int groups = (k + 63) >> 6;
+  const int num_tiles = (n_rows + kTileRows - 1) / kTileRows;
+
+  float4* xs = reinterpret_cast<float4*>(smem_raw + size_t(stages) * stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xs + (k >> 2));
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_empty = bar_full + 8 * stages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * stages);
+  float* red_v = reinterpret_cast<float*>(bars + 2 * stages + 1);
+  int* red_i = reinterpret_cast<int*>(red_v + kConsumerWarps);
+
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, kConsumerWarps);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const unsigned char* wbase = static_cast<const unsigned char*>(weight);
+      int i = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
+        if (!mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1, abort_flag,
+                               B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status))
+          break;
+        const int row0 = tile * kTileRows;
+        const int rows = min(kTileRows, n_rows - row0);
+        const uint32_t wbytes = uint32_t(rows) * row_bytes;
+        const uint32_t sbytes = kW8 ? uint32_t(rows) * groups * 2 : 0u;
+        unsigned char* st = smem_raw + size_t(s) * stage_bytes;
+        mbar_arrive_expect_tx(bar_full + 8 * s, wbytes + sbytes);
+        bulk_load(smem_u32(st), wbase + size_t(row0) * row_bytes, wbytes,
+                  bar_full + 8 * s);
+        if (kW8) {
+          bulk_load(smem_u32(st + w_tile_bytes), scales + size_t(row0) * groups,
+                    sbytes, bar_full + 8 * s);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int ct = threadIdx.x - 32;  // 0 .. 255
+    pdl_wait_primary();
+    // x -> FP32 planes: xs[p * chunks + c] = x[c*kEPC + 4p .. +3].
+    for (int e4 = ct; e4 < (k >> 2); e4 += kConsumerWarps * 32) {
+      const uint2 raw = reinterpret_cast<const uint2*>(input)[e4];
+      const int c = (e4 * 4) / kEPC;
+      const int p = ((e4 * 4) % kEPC) >> 2;
+      xs[p * chunks + c] = make_float4(bf16_lo(raw.x), bf16_hi(raw.x),
+                                       bf16_lo(raw.y), bf16_hi(raw.y));
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+
+    const int rloc0 = (warp - 1) * kR;
+    float best = -FLT_MAX;
+    int best_index = INT_MAX;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+      const int s = i % stages;
+      const uint32_t ph = (i / stages) & 1;
+      if (!mbar_wait_bounded(bar_full + 8 * s, ph, abort_flag,
+                             B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status))
+        break;
+      const unsigned char* wt = smem_raw + size_t(s) * stage_bytes;
+      const bf16* stile = reinterpret_cast<const bf16*>(wt + w_tile_bytes);
+      float acc[kR];
+      float2 acc2[kR];
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        acc[r] = 0.0f;
+        acc2[r] = f2(0.0f, 0.0f);
+      }
+      for (int c = lane; c < chunks; c += 32) {
+        float4 xv[kPlanes];
+#pragma unroll
+        for (int p = 0; p < kPlanes; ++p) xv[p] = xs[p * chunks + c];
+#pragma unroll
+        for (int r = 0; r < kR; ++r) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(
+              wt + (rloc0 + r) * row_bytes + c * 16);
+          if constexpr (kW8) {
+            float2 a = f2(0.0f, 0.0f);
+            a = dot4_s8_x2(wv.x, xv[0], a);
+            a = dot4_s8_x2(wv.y, xv[1], a);
+            a = dot4_s8_x2(wv.z, xv[2], a);
+            a = dot4_s8_x2(wv.w, xv[3], a);
+            const float sc =
+                __bfloat162float(stile[(rloc0 + r) * groups + (c >> 2)]);
+            acc[r] = fmaf(a.x + a.y, sc, acc[r]);
+          } else {
+            acc2[r] = dot4_bf16_x2(wv.x, wv.y, xv[0], acc2[r]);
+            acc2[r] = dot4_bf16_x2(wv.z, wv.w, xv[1], acc2[r]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * s);
+      const int row0 = tile * kTileRows + rloc0;
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        float v = kW8 ? acc[r] : acc2[r].x + acc2[r].y;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          v += __shfl_xor_sync(0xffffffffu, v, off);
+        }
+        const int row = row0 + r;
+        if (lane == 0 && row < n_rows) {
+          const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
+          const bf16 y = __float2bfloat16_rn(v + b);
+          output[row] = y;
+          argmax_update(best, best_index, __bfloat162float(y), row);
+        }
+      }
+    }
+    if (block_value != nullptr) {
+      if (lane == 0) {
+        red_v[warp - 1] = best;
+        red_i[warp - 1] = best_index;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      if (ct == 0) {
+        float b = -FLT_MAX;
+        int bi = INT_MAX;
+        for (int w = 0; w < kConsumerWarps; ++w) argmax_update(b, bi, red_v[w], red_i[w]);
+        block_value[blockIdx.x] = b;
+        block_index[blockIdx.x] = bi;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+struct BulkPlan {
+  int r = 0;  // rows per consumer warp (0: plan not possible)
+  int stages = 0;
+  int stage_bytes = 0;
+  int w_tile_bytes = 0;
+  int smem = 0;
+  int grid = 0;
+};
+
+int device_sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int count = 148;
+  cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+  return count;
+}
+
+BulkPlan plan_bulk(bool w8, int n, int k) {
+  BulkPlan p;
+  const int sms = device_sm_count();
+  const int row_bytes = w8 ? k : 2 * k;
+  const int groups = (k + 63) / 64;
+  int r = 1;
+  if ((n + 31) / 32 >= 2 * sms) {
+    r = 4;
+  } else if ((n + 15) / 16 >= sms) {
+    r = 2;
+  }
+  const int x_bytes = k * 4;
+  for (; r >= 1; r >>= 1) {
+    const int rows = kConsumerWarps * r;
+    const int wt = rows * row_bytes;
+    const int st = (wt + (w8 ? rows * groups * 2 : 0) + 127) / 128 * 128;
+    const int budget = kBulkSmemBudget - x_bytes - 256;
+    const int stages = budget / st < kMaxStages ? budget / st : kMaxStages;
+    if (stages >= 2) {
+      p.r = r;
+      p.stages = stages;
+      p.stage_bytes = st;
+      p.w_tile_bytes = wt;
+      p.smem = stages * st + x_bytes + 8 * 2 * stages + 8 + 8 * kConsumerWarps;
+      const int tiles = (n + rows - 1) / rows;
+      p.grid = tiles < sms ? tiles : sms;
+      return p;
+    }
+  }
+  return p;
+}
+
+template <bool kW8, int kR>
+cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
+                        const bf16* b, const bf16* x, bf16* y, int n, int k,
+                        float* bv, int* bi, cudaStream_t stream) {
+  auto kernel = gemv_bulk_kernel<kW8, kR>;
+  cudaError_t e = cudaFuncSetAttribute(
+      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kBulkThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, w, s, b, x, y, n, k, p.stages,
+                            p.stage_bytes, p.w_tile_bytes, bv, bi);
+}
+
 struct GemvConfig {
   int tpr;  // threads per team
   int r;    // rows per team
@@ -491,6 +770,27 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
                                       k, block_value, block_index, stream,
                                       grid_out);
   }
+  // TMA-bulk path: needs whole 8-row tiles of 16-byte multiples (n % 8) and
+  // 16-byte aligned scales.
+  const bool bulk_ok = n % 8 == 0 && (!w8 || aligned16(scales));
+  if (bulk_ok) {
+    const BulkPlan p = plan_bulk(w8, n, k);
+    if (p.r > 0) {
+      if (grid_out) *grid_out = p.grid;
+      if (w8) {
+        switch (p.r) {
+          case 4: return launch_bulk<true, 4>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
+          case 2: return launch_bulk<true, 2>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
+          default: return launch_bulk<true, 1>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
+        }
+      }
+      switch (p.r) {
+        case 4: return launch_bulk<false, 4>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
+        case 2: return launch_bulk<false, 2>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
+        default: return launch_bulk<false, 1>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
+      }
+    }
+  }
   const int chunks = w8 ? k / 16 : k / 8;
   const GemvConfig c = choose_config(n, chunks, block_value != nullptr);
   if (w8) {
@@ -507,6 +807,13 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
                   : dispatch_tpr<false, 1>(c.tpr, weight, scales, bias, input,
                                            output, n, k, block_value,
                                            block_index, stream, grid_out);
+}
+
+cudaError_t read_gemv_status(int* value, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_gemv_status, sizeof(int));
+  if (e != cudaSuccess || !clear) return e;
+  const int zero = 0;
+  return cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
 }
 
 cudaError_t launch_argmax_partials(const float* block_value,
