@@ -399,7 +399,7 @@ argmax_bf16_kernel(const bf16* __restrict__ values, int n,
 // 4p..4p+3 of every chunk) so that consecutive lanes read consecutive
 // 16-byte words (no bank conflicts).  The INT8 products use the sm_100
 // packed FP32 instructions (2 elements per FADD2 / FFMA2).
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kBulkThreads = 32 * (kConsumerWarps + 1);
 constexpr int kBulkSmemBudget = 200 * 1024;
 constexpr int kMaxStages = 6;
@@ -433,7 +433,15 @@ __device__ __forceinline__ float2 dot4_bf16_x2(uint32_t w01, uint32_t w23,
   return a;
 }
 
-template <bool kW8, int kR>
+// Tile geometry.  kWPR == 1: kConsumerWarps warps x (32 / kLPR) row groups
+// per warp x kR rows per lane group; a row is covered by kLPR lanes (16-byte
+// chunks c = l, l + kLPR, ...), kLPR chosen per shape so that the chunk
+// count divides evenly (896 INT8 = 56 chunks -> 8 lanes); the row groups of
+// a warp read the same x words, which shared memory broadcasts.
+// kWPR > 1 (small / long-K matrices, to put more SMs on the stream): each
+// row is split across kWPR warps of 32 lanes, whose partial sums meet in
+// shared memory once per tile.
+template <bool kW8, int kLPR, int kR, int kWPR>
 __global__ void __launch_bounds__(kBulkThreads, 1)
 gemv_bulk_kernel(const void* __restrict__ weight,
                  const bf16* __restrict__ scales,
@@ -444,7 +452,11 @@ gemv_bulk_kernel(const void* __restrict__ weight,
                  int* __restrict__ block_index) {
   constexpr int kEPC = kW8 ? 16 : 8;  // elements per 16-byte chunk
   constexpr int kPlanes = kEPC / 4;
-  constexpr int kTileRows = kConsumerWarps * kR;
+  static_assert(kWPR == 1 || (kLPR == 32 && kR == 1), "split rows use whole warps");
+  constexpr int kGroups = kWPR > 1 ? 1 : 32 / kLPR;  // row groups per warp
+  constexpr int kWarpRows = kGroups * kR;
+  constexpr int kTileRows =
+      kWPR > 1 ? kConsumerWarps / kWPR : kConsumerWarps * kWarpRows;
   extern __shared__ __align__(128) unsigned char smem_raw[];
 
   const int warp = threadIdx.x >> 5;
@@ -461,6 +473,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * stages);
   float* red_v = reinterpret_cast<float*>(bars + 2 * stages + 1);
   int* red_i = reinterpret_cast<int*>(red_v + kConsumerWarps);
+  float* red_part = reinterpret_cast<float*>(red_i + kConsumerWarps);  // [2][warps]
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
@@ -499,7 +512,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const int ct = threadIdx.x - 32;  // 0 .. 255
+    const int ct = threadIdx.x - 32;
     pdl_wait_primary();
     // x -> FP32 planes: xs[p * chunks + c] = x[c*kEPC + 4p .. +3].
     for (int e4 = ct; e4 < (k >> 2); e4 += kConsumerWarps * 32) {
@@ -511,7 +524,12 @@ gemv_bulk_kernel(const void* __restrict__ weight,
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
-    const int rloc0 = (warp - 1) * kR;
+    const int cw = warp - 1;                  // consumer warp index
+    const int gl = lane / kLPR;               // row group within the warp
+    const int ll = lane % kLPR;               // lane within the row group
+    const int ksub = kWPR > 1 ? cw % kWPR : 0;  // K slice of a split row
+    const int rloc0 =
+        kWPR > 1 ? cw / kWPR : cw * kWarpRows + gl * kR;
     float best = -FLT_MAX;
     int best_index = INT_MAX;
     int i = 0;
@@ -530,7 +548,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         acc[r] = 0.0f;
         acc2[r] = f2(0.0f, 0.0f);
       }
-      for (int c = lane; c < chunks; c += 32) {
+      for (int c = ksub * kLPR + ll; c < chunks; c += kLPR * kWPR) {
         float4 xv[kPlanes];
 #pragma unroll
         for (int p = 0; p < kPlanes; ++p) xv[p] = xs[p * chunks + c];
@@ -560,11 +578,23 @@ gemv_bulk_kernel(const void* __restrict__ weight,
       for (int r = 0; r < kR; ++r) {
         float v = kW8 ? acc[r] : acc2[r].x + acc2[r].y;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
+        for (int off = kLPR / 2; off > 0; off >>= 1) {
           v += __shfl_xor_sync(0xffffffffu, v, off);
         }
+        if constexpr (kWPR > 1) {
+          // Partials of the kWPR warps of a row meet in shared memory
+          // (double-buffered by tile parity: one barrier per tile).
+          float* part = red_part + (i & 1) * kConsumerWarps;
+          if (lane == 0) part[cw] = v;
+          asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+          if (ksub == 0) {
+            v = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kWPR; ++j) v += part[cw + j];
+          }
+        }
         const int row = row0 + r;
-        if (lane == 0 && row < n_rows) {
+        if (ll == 0 && ksub == 0 && row < n_rows) {
           const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
           const bf16 y = __float2bfloat16_rn(v + b);
           output[row] = y;
@@ -573,6 +603,12 @@ gemv_bulk_kernel(const void* __restrict__ weight,
       }
     }
     if (block_value != nullptr) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_index, off);
+        argmax_update(best, best_index, ov, oi);
+      }
       if (lane == 0) {
         red_v[warp - 1] = best;
         red_i[warp - 1] = best_index;
@@ -591,7 +627,9 @@ gemv_bulk_kernel(const void* __restrict__ weight,
 }
 
 struct BulkPlan {
-  int r = 0;  // rows per consumer warp (0: plan not possible)
+  int lpr = 0;  // lanes per row (0: plan not possible)
+  int r = 0;    // rows per lane group
+  int wpr = 1;  // warps per row
   int stages = 0;
   int stage_bytes = 0;
   int w_tile_bytes = 0;
@@ -607,43 +645,58 @@ int device_sm_count() {
   return count;
 }
 
+// Chooses the tile geometry by a simple cost model: rows streamed by the
+// busiest SM (waves x rows per tile), divided by the fraction of lanes doing
+// useful work in the chunk loop, plus a small charge per tile for the
+// cross-warp reduction of split rows.  Large matrices get 8-lane rows with
+// no split; small or long-K ones get split rows that reach every SM.
 BulkPlan plan_bulk(bool w8, int n, int k) {
-  BulkPlan p;
+  BulkPlan best;
+  double best_cost = 1e30;
   const int sms = device_sm_count();
   const int row_bytes = w8 ? k : 2 * k;
   const int groups = (k + 63) / 64;
-  int r = 1;
-  if ((n + 31) / 32 >= 2 * sms) {
-    r = 4;
-  } else if ((n + 15) / 16 >= sms) {
-    r = 2;
-  }
+  const int chunks = w8 ? k / 16 : k / 8;
   const int x_bytes = k * 4;
-  for (; r >= 1; r >>= 1) {
-    const int rows = kConsumerWarps * r;
+  const int budget = kBulkSmemBudget - x_bytes - 512;
+  struct Cand { int lpr, r, wpr; };
+  const Cand cands[] = {{8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1}, {32, 2, 1},
+                        {32, 1, 1}, {32, 1, 2}, {32, 1, 4}};
+  for (const Cand& c : cands) {
+    const int rows = c.wpr > 1 ? kConsumerWarps / c.wpr
+                               : kConsumerWarps * (32 / c.lpr) * c.r;
     const int wt = rows * row_bytes;
     const int st = (wt + (w8 ? rows * groups * 2 : 0) + 127) / 128 * 128;
-    const int budget = kBulkSmemBudget - x_bytes - 256;
     const int stages = budget / st < kMaxStages ? budget / st : kMaxStages;
-    if (stages >= 2) {
-      p.r = r;
-      p.stages = stages;
-      p.stage_bytes = st;
-      p.w_tile_bytes = wt;
-      p.smem = stages * st + x_bytes + 8 * 2 * stages + 8 + 8 * kConsumerWarps;
-      const int tiles = (n + rows - 1) / rows;
-      p.grid = tiles < sms ? tiles : sms;
-      return p;
+    if (stages < 2) continue;
+    const int span = c.lpr * c.wpr;
+    const int iters = (chunks + span - 1) / span;
+    const double eff = double(chunks) / double(iters * span);
+    const int tiles = (n + rows - 1) / rows;
+    const int waves = (tiles + sms - 1) / sms;
+    const double cost = double(waves) * rows * row_bytes / eff +
+                        (c.wpr > 1 ? waves * 2048.0 : 0.0);
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best.lpr = c.lpr;
+      best.r = c.r;
+      best.wpr = c.wpr;
+      best.stages = stages;
+      best.stage_bytes = st;
+      best.w_tile_bytes = wt;
+      best.smem = stages * st + x_bytes + 8 * 2 * stages + 8 +
+                  8 * kConsumerWarps + 8 * kConsumerWarps;
+      best.grid = tiles < sms ? tiles : sms;
     }
   }
-  return p;
+  return best;
 }
 
-template <bool kW8, int kR>
+template <bool kW8, int kLPR, int kR, int kWPR>
 cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                         const bf16* b, const bf16* x, bf16* y, int n, int k,
                         float* bv, int* bi, cudaStream_t stream) {
-  auto kernel = gemv_bulk_kernel<kW8, kR>;
+  auto kernel = gemv_bulk_kernel<kW8, kLPR, kR, kWPR>;
   cudaError_t e = cudaFuncSetAttribute(
       kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
   if (e != cudaSuccess) return e;
@@ -659,6 +712,24 @@ cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, w, s, b, x, y, n, k, p.stages,
                             p.stage_bytes, p.w_tile_bytes, bv, bi);
+}
+
+template <bool kW8>
+cudaError_t dispatch_bulk(const BulkPlan& p, const void* w, const bf16* s,
+                          const bf16* b, const bf16* x, bf16* y, int n, int k,
+                          float* bv, int* bi, cudaStream_t st) {
+  if (p.wpr == 4) return launch_bulk<kW8, 32, 1, 4>(p, w, s, b, x, y, n, k, bv, bi, st);
+  if (p.wpr == 2) return launch_bulk<kW8, 32, 1, 2>(p, w, s, b, x, y, n, k, bv, bi, st);
+  if (p.lpr == 8) {
+    return p.r == 2 ? launch_bulk<kW8, 8, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
+                    : launch_bulk<kW8, 8, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
+  }
+  if (p.lpr == 16) {
+    return p.r == 2 ? launch_bulk<kW8, 16, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
+                    : launch_bulk<kW8, 16, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
+  }
+  return p.r == 2 ? launch_bulk<kW8, 32, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
+                  : launch_bulk<kW8, 32, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
 }
 
 struct GemvConfig {
@@ -775,20 +846,12 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
   const bool bulk_ok = n % 8 == 0 && (!w8 || aligned16(scales));
   if (bulk_ok) {
     const BulkPlan p = plan_bulk(w8, n, k);
-    if (p.r > 0) {
+    if (p.lpr > 0) {
       if (grid_out) *grid_out = p.grid;
-      if (w8) {
-        switch (p.r) {
-          case 4: return launch_bulk<true, 4>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
-          case 2: return launch_bulk<true, 2>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
-          default: return launch_bulk<true, 1>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
-        }
-      }
-      switch (p.r) {
-        case 4: return launch_bulk<false, 4>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
-        case 2: return launch_bulk<false, 2>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
-        default: return launch_bulk<false, 1>(p, weight, scales, bias, input, output, n, k, block_value, block_index, stream);
-      }
+      return w8 ? dispatch_bulk<true>(p, weight, scales, bias, input, output, n,
+                                      k, block_value, block_index, stream)
+                : dispatch_bulk<false>(p, weight, scales, bias, input, output,
+                                       n, k, block_value, block_index, stream);
     }
   }
   const int chunks = w8 ? k / 16 : k / 8;

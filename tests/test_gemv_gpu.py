@@ -135,3 +135,27 @@ def test_gemv_unaligned_and_k_zero(b200, oracle, cuda):
     b200.gemv_bf16(dw, from_bits(bb, cuda), dx, y, n, 0)
     assert np.array_equal(to_bits(y), bb)
     assert b200.device_status() == 0
+
+
+@pytest.mark.parametrize("n,k", [(8, 64), (16, 128), (24, 896), (40, 4864), (1000, 896),
+                                 (2056, 1024), (4096, 2048), (512, 8192), (64, 12288),
+                                 (8, 30000)])
+@pytest.mark.parametrize("w8", [True, False])
+def test_gemv_tile_geometries(b200, oracle, cuda, n, k, w8):
+    """Partial tiles, split rows and the large-K fallbacks of the TMA path."""
+    import torch
+    w, _ = seeded_linear(n, k, seed=n * 31 + k)
+    x = oracle.f32_to_bf16(np.random.default_rng(n + k).standard_normal(k).astype(np.float32))
+    y = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+    if w8:
+        q, sb = oracle.quantize_groupwise(w)
+        b200.gemv_w8a16(torch.from_numpy(q).to(cuda), from_bits(sb, cuda), 64, None,
+                        from_bits(x, cuda), y, n, k)
+        exp = oracle.bf16_to_f32(oracle.linear_w8a16(q, sb, None, x, gemm=False))[0]
+    else:
+        wb = oracle.f32_to_bf16(w)
+        b200.gemv_bf16(from_bits(wb, cuda), None, from_bits(x, cuda), y, n, k)
+        exp = oracle.bf16_to_f32(oracle.f32_to_bf16(oracle.linear_bf16(wb, None, x)[0]))
+    got = oracle.bf16_to_f32(to_bits(y))
+    assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
+    assert b200.device_status() == 0
