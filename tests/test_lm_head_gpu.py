@@ -24,7 +24,7 @@ def run_lm_head(b200, cuda, w_dev, x_dev, vocab, k, scales=None):
 @pytest.mark.parametrize("vocab,hidden,tie_a,tie_b",
                          [(512, 64, 3, 4), (1002, 64, 7, 71), (200, 10, 5, 22),
                           (8, 4, 0, 3), (64, 896, 1, 31), (4096, 896, 70, 4000),
-                          (65536, 896, 30001, 30002), (151936, 896, 151935, 151934)])
+                          (65536, 896, 30001, 30002), (151936, 896, 151934, 151935)])
 def test_lm_head_ties_resolve_to_lowest_index(b200, oracle, cuda, vocab, hidden,
                                               tie_a, tie_b):
     w, x = lm_head_tie_case(vocab, hidden, tie_a, tie_b)
