@@ -441,13 +441,16 @@ __device__ __forceinline__ float2 dot4_bf16_x2(uint32_t w01, uint32_t w23,
 // kWPR > 1 (small / long-K matrices, to put more SMs on the stream): each
 // row is split across kWPR warps of 32 lanes, whose partial sums meet in
 // shared memory once per tile.
-template <bool kW8, int kLPR, int kR, int kWPR>
+// kK != 0 compiles the kernel for that in_features (the Qwen2.5 hidden size
+// 896): the chunk loop is fully unrolled and every shared-memory offset is
+// an immediate.  kK == 0 handles any in_features.
+template <bool kW8, int kLPR, int kR, int kWPR, int kK>
 __global__ void __launch_bounds__(kBulkThreads, 1)
 gemv_bulk_kernel(const void* __restrict__ weight,
                  const bf16* __restrict__ scales,
                  const bf16* __restrict__ bias,
                  const bf16* __restrict__ input, bf16* __restrict__ output,
-                 int n_rows, int k, int stages, int stage_bytes,
+                 int n_rows, int k_arg, int stages, int stage_bytes,
                  int w_tile_bytes, float* __restrict__ block_value,
                  int* __restrict__ block_index) {
   constexpr int kEPC = kW8 ? 16 : 8;  // elements per 16-byte chunk
@@ -461,10 +464,17 @@ gemv_bulk_kernel(const void* __restrict__ weight,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int k = kK != 0 ? kK : k_arg;
   const int row_bytes = kW8 ? k : 2 * k;
   const int chunks = k / kEPC;
   const int groups = (k + 63) >> 6;
   const int num_tiles = (n_rows + kTileRows - 1) / kTileRows;
+  // Chunk iterations per lane when kK is known (with a bound check if the
+  // lanes do not divide the chunks evenly).
+  constexpr int kChunks = kK / kEPC;
+  constexpr int kSpan = kLPR * kWPR;
+  constexpr int kIters = kK != 0 ? (kChunks + kSpan - 1) / kSpan : 0;
+  constexpr bool kExact = kK != 0 && kChunks % kSpan == 0;
 
   float4* xs = reinterpret_cast<float4*>(smem_raw + size_t(stages) * stage_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(xs + (k >> 2));
@@ -548,7 +558,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         acc[r] = 0.0f;
         acc2[r] = f2(0.0f, 0.0f);
       }
-      for (int c = ksub * kLPR + ll; c < chunks; c += kLPR * kWPR) {
+      auto chunk_step = [&](int c) {
         float4 xv[kPlanes];
 #pragma unroll
         for (int p = 0; p < kPlanes; ++p) xv[p] = xs[p * chunks + c];
@@ -570,6 +580,17 @@ gemv_bulk_kernel(const void* __restrict__ weight,
             acc2[r] = dot4_bf16_x2(wv.z, wv.w, xv[1], acc2[r]);
           }
         }
+      };
+      const int c0 = ksub * kLPR + ll;
+      if constexpr (kK != 0) {
+#pragma unroll
+        for (int j = 0; j < kIters; ++j) {
+          const int c = c0 + j * kSpan;
+          if (kExact || c < kChunks) chunk_step(c);
+        }
+      } else {
+#pragma unroll 2
+        for (int c = c0; c < chunks; c += kSpan) chunk_step(c);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_empty + 8 * s);
@@ -645,12 +666,13 @@ int device_sm_count() {
   return count;
 }
 
-// Chooses the tile geometry by a simple cost model: rows streamed by the
+// Chooses the tile geometry (tiles of at least min_rows rows) by a simple
+// cost model: rows streamed by the
 // busiest SM (waves x rows per tile), divided by the fraction of lanes doing
 // useful work in the chunk loop, plus a small charge per tile for the
 // cross-warp reduction of split rows.  Large matrices get 8-lane rows with
 // no split; small or long-K ones get split rows that reach every SM.
-BulkPlan plan_bulk(bool w8, int n, int k) {
+BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   BulkPlan best;
   double best_cost = 1e30;
   const int sms = device_sm_count();
@@ -665,6 +687,7 @@ BulkPlan plan_bulk(bool w8, int n, int k) {
   for (const Cand& c : cands) {
     const int rows = c.wpr > 1 ? kConsumerWarps / c.wpr
                                : kConsumerWarps * (32 / c.lpr) * c.r;
+    if (rows < min_rows) continue;
     const int wt = rows * row_bytes;
     const int st = (wt + (w8 ? rows * groups * 2 : 0) + 127) / 128 * 128;
     const int stages = budget / st < kMaxStages ? budget / st : kMaxStages;
@@ -696,7 +719,8 @@ template <bool kW8, int kLPR, int kR, int kWPR>
 cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                         const bf16* b, const bf16* x, bf16* y, int n, int k,
                         float* bv, int* bi, cudaStream_t stream) {
-  auto kernel = gemv_bulk_kernel<kW8, kLPR, kR, kWPR>;
+  auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896>
+                         : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0>;
   cudaError_t e = cudaFuncSetAttribute(
       kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
   if (e != cudaSuccess) return e;
@@ -845,7 +869,9 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
   // 16-byte aligned scales.
   const bool bulk_ok = n % 8 == 0 && (!w8 || aligned16(scales));
   if (bulk_ok) {
-    const BulkPlan p = plan_bulk(w8, n, k);
+    // The LM-head form writes one argmax partial per CTA into a workspace of
+    // ceil(n / 8) entries: tiles of >= 8 rows keep the grid within it.
+    const BulkPlan p = plan_bulk(w8, n, k, block_value != nullptr ? 8 : 1);
     if (p.lpr > 0) {
       if (grid_out) *grid_out = p.grid;
       return w8 ? dispatch_bulk<true>(p, weight, scales, bias, input, output, n,
