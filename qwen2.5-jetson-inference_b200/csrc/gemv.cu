@@ -667,11 +667,12 @@ int device_sm_count() {
 }
 
 // Chooses the tile geometry (tiles of at least min_rows rows) by a simple
-// cost model: rows streamed by the
-// busiest SM (waves x rows per tile), divided by the fraction of lanes doing
-// useful work in the chunk loop, plus a small charge per tile for the
-// cross-warp reduction of split rows.  Large matrices get 8-lane rows with
-// no split; small or long-K ones get split rows that reach every SM.
+// cost model: bytes streamed by the busiest SM (waves x tile bytes), divided
+// by the fraction of lanes doing useful work in the chunk loop, times a
+// shared-memory factor for INT8 rows (each product also reads 4/r bytes of
+// x), plus a small charge per tile for the cross-warp reduction of split
+// rows.  Large INT8 matrices get 4 rows per lane; small or long-K ones get
+// split rows that reach every SM.
 BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   BulkPlan best;
   double best_cost = 1e30;
@@ -682,8 +683,8 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   const int x_bytes = k * 4;
   const int budget = kBulkSmemBudget - x_bytes - 512;
   struct Cand { int lpr, r, wpr; };
-  const Cand cands[] = {{8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1}, {32, 2, 1},
-                        {32, 1, 1}, {32, 1, 2}, {32, 1, 4}};
+  const Cand cands[] = {{32, 4, 1}, {8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1},
+                        {32, 2, 1}, {32, 1, 1}, {32, 1, 2}, {32, 1, 4}};
   for (const Cand& c : cands) {
     const int rows = c.wpr > 1 ? kConsumerWarps / c.wpr
                                : kConsumerWarps * (32 / c.lpr) * c.r;
@@ -697,7 +698,8 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
     const double eff = double(chunks) / double(iters * span);
     const int tiles = (n + rows - 1) / rows;
     const int waves = (tiles + sms - 1) / sms;
-    const double cost = double(waves) * rows * row_bytes / eff +
+    const double smem_factor = w8 ? 1.0 + 0.5 / c.r : 1.0;
+    const double cost = double(waves) * rows * row_bytes / eff * smem_factor +
                         (c.wpr > 1 ? waves * 2048.0 : 0.0);
     if (cost < best_cost * 0.999) {
       best_cost = cost;
@@ -752,6 +754,7 @@ cudaError_t dispatch_bulk(const BulkPlan& p, const void* w, const bf16* s,
     return p.r == 2 ? launch_bulk<kW8, 16, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
                     : launch_bulk<kW8, 16, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
   }
+  if (p.r == 4) return launch_bulk<kW8, 32, 4, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
   return p.r == 2 ? launch_bulk<kW8, 32, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
                   : launch_bulk<kW8, 32, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
 }
