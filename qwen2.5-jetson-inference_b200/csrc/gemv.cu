@@ -499,10 +499,11 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   if (warp == 0) {
     if (lane == 0) {
       const unsigned char* wbase = static_cast<const unsigned char*>(weight);
-      int i = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
-        const int s = i % stages;
-        const uint32_t ph = (i / stages) & 1;
+      int i = 0, s = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < num_tiles;
+           tile += gridDim.x, ++i, s = (s + 1 == stages ? 0 : s + 1),
+               ph ^= (s == 0 ? 1u : 0u)) {
         if (!mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1, abort_flag,
                                B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status))
           break;
@@ -542,22 +543,19 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         kWPR > 1 ? cw / kWPR : cw * kWarpRows + gl * kR;
     float best = -FLT_MAX;
     int best_index = INT_MAX;
-    int i = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
-      const int s = i % stages;
-      const uint32_t ph = (i / stages) & 1;
+    int i = 0, s = 0;
+    uint32_t ph = 0;
+    for (int tile = blockIdx.x; tile < num_tiles;
+         tile += gridDim.x, ++i, s = (s + 1 == stages ? 0 : s + 1),
+             ph ^= (s == 0 ? 1u : 0u)) {
       if (!mbar_wait_bounded(bar_full + 8 * s, ph, abort_flag,
                              B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status))
         break;
       const unsigned char* wt = smem_raw + size_t(s) * stage_bytes;
       const bf16* stile = reinterpret_cast<const bf16*>(wt + w_tile_bytes);
-      float acc[kR];
       float2 acc2[kR];
 #pragma unroll
-      for (int r = 0; r < kR; ++r) {
-        acc[r] = 0.0f;
-        acc2[r] = f2(0.0f, 0.0f);
-      }
+      for (int r = 0; r < kR; ++r) acc2[r] = f2(0.0f, 0.0f);
       auto chunk_step = [&](int c) {
         float4 xv[kPlanes];
 #pragma unroll
@@ -567,14 +565,18 @@ gemv_bulk_kernel(const void* __restrict__ weight,
           const uint4 wv = *reinterpret_cast<const uint4*>(
               wt + (rloc0 + r) * row_bytes + c * 16);
           if constexpr (kW8) {
+            // Two independent chains of the chunk's 16 products, each then
+            // scaled into the row accumulator with one packed FMA.
             float2 a = f2(0.0f, 0.0f);
+            float2 b = f2(0.0f, 0.0f);
             a = dot4_s8_x2(wv.x, xv[0], a);
-            a = dot4_s8_x2(wv.y, xv[1], a);
+            b = dot4_s8_x2(wv.y, xv[1], b);
             a = dot4_s8_x2(wv.z, xv[2], a);
-            a = dot4_s8_x2(wv.w, xv[3], a);
+            b = dot4_s8_x2(wv.w, xv[3], b);
             const float sc =
                 __bfloat162float(stile[(rloc0 + r) * groups + (c >> 2)]);
-            acc[r] = fmaf(a.x + a.y, sc, acc[r]);
+            acc2[r] = __ffma2_rn(a, f2(sc, sc), acc2[r]);
+            acc2[r] = __ffma2_rn(b, f2(sc, sc), acc2[r]);
           } else {
             acc2[r] = dot4_bf16_x2(wv.x, wv.y, xv[0], acc2[r]);
             acc2[r] = dot4_bf16_x2(wv.z, wv.w, xv[1], acc2[r]);
@@ -597,7 +599,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
       const int row0 = tile * kTileRows + rloc0;
 #pragma unroll
       for (int r = 0; r < kR; ++r) {
-        float v = kW8 ? acc[r] : acc2[r].x + acc2[r].y;
+        float v = acc2[r].x + acc2[r].y;
 #pragma unroll
         for (int off = kLPR / 2; off > 0; off >>= 1) {
           v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -668,11 +670,11 @@ int device_sm_count() {
 
 // Chooses the tile geometry (tiles of at least min_rows rows) by a simple
 // cost model: bytes streamed by the busiest SM (waves x tile bytes), divided
-// by the fraction of lanes doing useful work in the chunk loop, times a
-// shared-memory factor for INT8 rows (each product also reads 4/r bytes of
-// x), plus a small charge per tile for the cross-warp reduction of split
-// rows.  Large INT8 matrices get 4 rows per lane; small or long-K ones get
-// split rows that reach every SM.
+// by the fraction of lanes doing useful work in the chunk loop (idle lanes
+// still cost issue slots, which bound the INT8 path), plus a small charge
+// per tile for the cross-warp reduction of split rows.  Large matrices get
+// rows whose chunks divide evenly among the lanes (896 INT8 -> 8 lanes);
+// small or long-K ones get split rows that reach every SM.
 BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   BulkPlan best;
   double best_cost = 1e30;
@@ -683,7 +685,7 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   const int x_bytes = k * 4;
   const int budget = kBulkSmemBudget - x_bytes - 512;
   struct Cand { int lpr, r, wpr; };
-  const Cand cands[] = {{32, 4, 1}, {8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1},
+  const Cand cands[] = {{8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1}, {32, 4, 1},
                         {32, 2, 1}, {32, 1, 1}, {32, 1, 2}, {32, 1, 4}};
   for (const Cand& c : cands) {
     const int rows = c.wpr > 1 ? kConsumerWarps / c.wpr
@@ -698,8 +700,7 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
     const double eff = double(chunks) / double(iters * span);
     const int tiles = (n + rows - 1) / rows;
     const int waves = (tiles + sms - 1) / sms;
-    const double smem_factor = w8 ? 1.0 + 0.5 / c.r : 1.0;
-    const double cost = double(waves) * rows * row_bytes / eff * smem_factor +
+    const double cost = double(waves) * rows * row_bytes / eff +
                         (c.wpr > 1 ? waves * 2048.0 : 0.0);
     if (cost < best_cost * 0.999) {
       best_cost = cost;
