@@ -6,7 +6,8 @@
  * src/cuda/kernels.cu:1540-1704).  Every entry point takes raw device
  * pointers, sizes and a CUDA stream; nothing here allocates device memory,
  * synchronises the stream, or keeps state between calls (except the
- * device-side error word read by b200_device_status).  All work is enqueued
+ * device-side error word read by b200_device_status and the fixed scratch
+ * array of b200_lm_head_bf16_noalloc).  All work is enqueued
  * asynchronously on `stream`, exactly like the reference functions.
  *
  * Layouts (reference conventions, src/qwen2.cpp:231-330):
@@ -131,6 +132,28 @@ int b200_lm_head_w8a16(const int8_t* weight, const uint16_t* scales,
  * src/cuda/kernels.cu:326-356, 1534-1538). */
 int b200_argmax_bf16(const uint16_t* values, int n, int* output,
                      b200_stream_t stream);
+
+/* Fused LM head that allocates nothing and needs no workspace.
+ * No counterpart in the reference (its lm_head_bf16 takes a caller-owned
+ * workspace).  For callers that cannot allocate device memory -- a plugin
+ * host that passes only inputs and outputs, or code already recording a CUDA
+ * graph, where cudaMalloc is not allowed -- the per-CTA argmax partials live
+ * in a fixed 256 KiB array in device memory owned by the library (one copy
+ * per GPU that loads the library, held until the process exits).  Same
+ * results as b200_lm_head_bf16.
+ *   - vocab must be <= b200_lm_head_noalloc_max_vocab() (262144);
+ *     larger returns B200_ERR_TOO_LARGE.
+ *   - The first call on a device looks up that device's copy of the array
+ *     (cudaGetSymbolAddress, with the device current); make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the one array: calls that may overlap on
+ *     the GPU (different streams without ordering) race on it; order them.
+ *   - No cudaMalloc, cudaFree or allocating library routine is called. */
+size_t b200_lm_head_noalloc_max_vocab(void);
+int b200_lm_head_bf16_noalloc(const uint16_t* weight, const uint16_t* bias,
+                              const uint16_t* input, uint16_t* logits,
+                              int* argmax, int vocab, int in_features,
+                              b200_stream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -42,6 +42,8 @@ _SIGNATURES = {
     "b200_lm_head_bf16": ([_p, _p, _p, _p, _p, _p, _p, _i, _i, _p], _i),
     "b200_lm_head_w8a16": ([_p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p], _i),
     "b200_argmax_bf16": ([_p, _i, _p, _p], _i),
+    "b200_lm_head_noalloc_max_vocab": ([], ctypes.c_size_t),
+    "b200_lm_head_bf16_noalloc": ([_p, _p, _p, _p, _p, _i, _i, _p], _i),
 }
 for _name, (_args, _res) in _SIGNATURES.items():
     _fn = getattr(_lib, _name)

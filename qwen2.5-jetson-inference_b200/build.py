@@ -21,7 +21,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libb200linear.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu"]
+SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
               "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
