@@ -398,6 +398,8 @@ def main():
     ap.add_argument("--passes", type=int, default=100, help="sweep passes per step")
     ap.add_argument("--no-gemm", action="store_true", help="skip the GEMM sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--only-gemm", action="store_true",
+                    help="run only the prefill GEMM sweep (configs[2])")
     ap.add_argument("--case", default=None,
                     help="profiling mode: run only one kernel, `--steps` launches "
                          "(gemv_w8, gemv_bf16, lm_head, gemm_w8, gemm_bf16)")
@@ -409,6 +411,11 @@ def main():
         return run_reference(args)
     if args.case:
         return run_case(args)
+    if args.only_gemm:
+        torch.cuda.set_device(0)
+        res = gemm_sweep(load_pkg(), torch.device("cuda", 0))
+        print(json.dumps({"gemm_sweep": res, "tile": os.environ.get("B200_GEMM_TILE")}))
+        return
 
     world, rank, local = init_dist()
     device = torch.device("cuda", local)

@@ -35,6 +35,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -355,20 +357,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     constexpr int kItems = kBN * 4;             // (row, 16-byte chunk) pairs
     constexpr int kPerThread = kItems / (C::kDqWarps * 32);
     static_assert(kItems % (C::kDqWarps * 32) == 0, "dequant split");
+    // Scales are read from global memory kAhead stages before they are
+    // needed (a register ring indexed by the unrolled loop position, so no
+    // load result is moved before it arrives): the L2 latency of the scale
+    // reads stays off the dequant critical path.
+    constexpr int kAhead = 4;
+    const uint16_t* sbits = reinterpret_cast<const uint16_t*>(scales);
+    auto load_scales = [&](int tile, int kb, uint32_t* out) {
+      const int nb = tile / num_m;
+#pragma unroll
+      for (int p = 0; p < kPerThread; ++p) {
+        const int item = dt + p * (C::kDqWarps * 32);
+        const int row = nb * kBN + (item >> 2);
+        const uint32_t v =
+            (tile < num_tiles && row < n) ? sbits[size_t(row) * groups + kb] : 0u;
+        out[p] = v | (v << 16);
+      }
+    };
+    int pf_tile = blockIdx.x, pf_kb = 0;
+    uint32_t sq[kAhead][kPerThread];
+#pragma unroll
+    for (int d = 0; d < kAhead; ++d) {
+      load_scales(pf_tile, pf_kb, sq[d]);
+      if (++pf_kb == num_kb) {
+        pf_kb = 0;
+        pf_tile += gridDim.x;
+      }
+    }
     int stage = 0;
     uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int nb = tile / num_m;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        // Scales of this k-block for my rows (issued before the wait).
-        float sc[kPerThread];
+    int tile = blockIdx.x, kb = 0;
+    const bf162 neg0 = __halves2bfloat162(__ushort_as_bfloat16(0x8000),
+                                          __ushort_as_bfloat16(0x8000));
+    while (true) {
 #pragma unroll
-        for (int p = 0; p < kPerThread; ++p) {
-          const int item = dt + p * (C::kDqWarps * 32);
-          const int row = nb * kBN + (item >> 2);
-          sc[p] = row < n ? __bfloat162float(scales[size_t(row) * groups + kb])
-                          : 0.0f;
-        }
+      for (int d = 0; d < kAhead; ++d) {
+        if (tile >= num_tiles) goto dequant_done;
         if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag,
                        B200_DEVICE_TIMEOUT_PIPELINE))
           goto dequant_done;
@@ -381,10 +405,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           const int r = item >> 2;
           const int j = item & 3;
           const uint4 raw = *reinterpret_cast<const uint4*>(qt + r * kBK + j * 16);
-          const bf16 sb = __float2bfloat16_rn(sc[p]);  // exact: sc is BF16
-          const bf162 s2 = __halves2bfloat162(sb, sb);
-          const bf162 neg0 = __halves2bfloat162(__ushort_as_bfloat16(0x8000),
-                                                __ushort_as_bfloat16(0x8000));
+          const uint32_t s2bits = sq[d][p];
+          const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
           uint32_t outw[8];
           const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
@@ -416,6 +438,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         if (++stage == C::kStages) {
           stage = 0;
           phase ^= 1;
+        }
+        // Refill this ring slot kAhead stages ahead.
+        load_scales(pf_tile, pf_kb, sq[d]);
+        if (++pf_kb == num_kb) {
+          pf_kb = 0;
+          pf_tile += gridDim.x;
+        }
+        if (++kb == num_kb) {
+          kb = 0;
+          tile += gridDim.x;
         }
       }
     }
@@ -508,6 +540,43 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+
+// Tile-shape choice: the largest tile that still gives every SM work.
+// B200_GEMM_TILE=256x128|128x256|128x128|128x64 overrides it (tuning only).
+enum class Tile { k256x128, k128x256, k128x128, k128x64 };
+
+Tile choose_tile(int m, int n) {
+  static const char* forced = getenv("B200_GEMM_TILE");
+  if (forced) {
+    if (!strcmp(forced, "256x128")) return Tile::k256x128;
+    if (!strcmp(forced, "128x256")) return Tile::k128x256;
+    if (!strcmp(forced, "128x128")) return Tile::k128x128;
+    if (!strcmp(forced, "128x64")) return Tile::k128x64;
+  }
+  const long long sms = sm_count();
+  const long long t256x128 = ((m + 255) / 256) * (long long)((n + 127) / 128);
+  const long long t128x128 = ((m + 127) / 128) * (long long)((n + 127) / 128);
+  if (t256x128 >= sms) return Tile::k256x128;
+  if (t128x128 >= sms / 2) return Tile::k128x128;
+  return Tile::k128x64;
+}
+
+template <bool kW8>
+cudaError_t launch_tile(Tile t, const void* weight, const bf16* scales,
+                        const bf16* bias, const bf16* input, bf16* output,
+                        int m, int n, int k, cudaStream_t stream) {
+  switch (t) {
+    case Tile::k256x128:
+      return launch_cfg<kW8, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
+    case Tile::k128x256:
+      return launch_cfg<kW8, 1, 256>(weight, scales, bias, input, output, m, n, k, stream);
+    case Tile::k128x128:
+      return launch_cfg<kW8, 1, 128>(weight, scales, bias, input, output, m, n, k, stream);
+    default:
+      return launch_cfg<kW8, 1, 64>(weight, scales, bias, input, output, m, n, k, stream);
+  }
+}
+
 }  // namespace
 
 bool gemm_tc_supported(bool w8, const void* weight, const void* input,
@@ -519,25 +588,12 @@ bool gemm_tc_supported(bool w8, const void* weight, const void* input,
   return get_encode_fn() != nullptr;
 }
 
-// Tile-shape choice: the largest tile that still gives every SM work.
 cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
                            const bf16* bias, const bf16* input, bf16* output,
                            int m, int n, int k, cudaStream_t stream) {
-  const long long sms = sm_count();
-  const long long tiles_256x128 = ((m + 255) / 256) * (long long)((n + 127) / 128);
-  const long long tiles_128x128 = ((m + 127) / 128) * (long long)((n + 127) / 128);
-  if (w8) {
-    if (tiles_256x128 >= sms)
-      return launch_cfg<true, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
-    if (tiles_128x128 >= sms / 2)
-      return launch_cfg<true, 1, 128>(weight, scales, bias, input, output, m, n, k, stream);
-    return launch_cfg<true, 1, 64>(weight, scales, bias, input, output, m, n, k, stream);
-  }
-  if (tiles_256x128 >= sms)
-    return launch_cfg<false, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
-  if (tiles_128x128 >= sms / 2)
-    return launch_cfg<false, 1, 128>(weight, scales, bias, input, output, m, n, k, stream);
-  return launch_cfg<false, 1, 64>(weight, scales, bias, input, output, m, n, k, stream);
+  const Tile t = choose_tile(m, n);
+  return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, stream)
+            : launch_tile<false>(t, weight, scales, bias, input, output, m, n, k, stream);
 }
 
 }  // namespace b200
