@@ -545,7 +545,10 @@ bool aligned16(const void* p) {
 // B200_GEMM_TILE=256x128|128x256|128x128|128x64 overrides it (tuning only).
 enum class Tile { k256x128, k128x256, k128x128, k128x64 };
 
-Tile choose_tile(int m, int n) {
+// BF16 prefers 128x256 (one N=256 MMA per k-step reads less shared memory
+// per FLOP than two M=128 x N=128 MMAs); INT8 weights prefer 256x128, which
+// dequantises each weight tile once for 256 token rows.
+Tile choose_tile(bool w8, int m, int n) {
   static const char* forced = getenv("B200_GEMM_TILE");
   if (forced) {
     if (!strcmp(forced, "256x128")) return Tile::k256x128;
@@ -556,6 +559,8 @@ Tile choose_tile(int m, int n) {
   const long long sms = sm_count();
   const long long t256x128 = ((m + 255) / 256) * (long long)((n + 127) / 128);
   const long long t128x128 = ((m + 127) / 128) * (long long)((n + 127) / 128);
+  const long long t128x256 = ((m + 127) / 128) * (long long)((n + 255) / 256);
+  if (!w8 && t128x256 >= sms) return Tile::k128x256;
   if (t256x128 >= sms) return Tile::k256x128;
   if (t128x128 >= sms / 2) return Tile::k128x128;
   return Tile::k128x64;
@@ -591,7 +596,7 @@ bool gemm_tc_supported(bool w8, const void* weight, const void* input,
 cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
                            const bf16* bias, const bf16* input, bf16* output,
                            int m, int n, int k, cudaStream_t stream) {
-  const Tile t = choose_tile(m, n);
+  const Tile t = choose_tile(w8, m, n);
   return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, stream)
             : launch_tile<false>(t, weight, scales, bias, input, output, m, n, k, stream);
 }
