@@ -252,6 +252,79 @@ def gemm_sweep(b200, device, reps=10):
     return res
 
 
+def sharded_bench(b200, world, rank, device, reps=5):
+    """column-sharded W8A16 GEMM (M=8192; K,N = 8192,28672 and
+    28672,8192) with the NCCL all-gather, and the vocabulary-sharded LM head
+    (896 -> 151936, M=1) with the cross-GPU argmax.  Device time, max over
+    ranks; TFLOP/s counts the whole (unsharded) GEMM."""
+    import importlib
+    sh = importlib.import_module("qwen25_b200.sharded")
+    comm = (sh.Comm.from_process_group() if world > 1
+            else sh.Comm(sh.new_unique_id(), 1, 0))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(100 + rank)
+    out = {"gemm": [], "lm_head": None}
+    m = 8192
+    for (k, n) in [(8192, 28672), (28672, 8192)]:
+        r0, nr = sh.shard_range(n, world, rank)
+        w = torch.randn(nr, k, generator=gen, device=device) * 0.02
+        q, s = b200.quantize_groupwise(w)
+        del w
+        xg = torch.Generator(device=device)
+        xg.manual_seed(7)  # X replicated: same seed on every rank
+        x = torch.randn(m, k, generator=xg, device=device).to(torch.bfloat16)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+        ws = sh.gemm_workspace(m, n, world, device)
+        yl = torch.empty(m, nr, dtype=torch.bfloat16, device=device)
+
+        def full():
+            sh.gemm_w8a16_allgather(comm, q, s, None, x, y, ws, m, n, k)
+
+        def local():
+            b200.gemm_w8a16(q, s, 64, None, x, yl, m, nr, k)
+
+        res = {"m": m, "k": k, "n": n}
+        for name, fn in (("sharded", full), ("local_gemm", local)):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            barrier(world)
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            t = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
+            res[name + "_ms"] = round(t * 1e3, 3)
+        res["tflops"] = round(2.0 * m * n * k / (res["sharded_ms"] / 1e3) / 1e12, 1)
+        out["gemm"].append(res)
+        del q, s, x, y, ws, yl
+        torch.cuda.empty_cache()
+    v, k = 151936, 896
+    v0, vn = sh.shard_range(v, world, rank)
+    wl = (torch.randn(vn, k, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    xl = torch.randn(k, generator=gen, device=device).to(torch.bfloat16)
+    logits = torch.empty(vn, dtype=torch.bfloat16, device=device)
+    wsl = sh.lm_head_workspace(v, world, device)
+    am = torch.empty(1, dtype=torch.int32, device=device)
+    for _ in range(3):
+        sh.lm_head_bf16(comm, wl, None, xl, logits, wsl, am, v, k)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(20):
+        sh.lm_head_bf16(comm, wl, None, xl, logits, wsl, am, v, k)
+    e1.record()
+    torch.cuda.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) / 1e3 / 20, world)
+    out["lm_head"] = {"vocab": v, "k": k, "us": round(t * 1e6, 2),
+                      "gbs_per_gpu": round(2 * (v // world) * k / t / 1e9, 1)}
+    comm.close()
+    return out
+
+
 # ------------------------------------------------------------ CPU reference
 def cpu_reference_sample(steps, warmup, budget_s=12.0):
     """Reference src/cpu_ops.cpp linear_fp32 (OpenBLAS sgemv, FP32 weights) on
@@ -398,6 +471,8 @@ def main():
     ap.add_argument("--passes", type=int, default=100, help="sweep passes per step")
     ap.add_argument("--no-gemm", action="store_true", help="skip the GEMM sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded GEMM / LM head (configs[4])")
     ap.add_argument("--only-gemm", action="store_true",
                     help="run only the prefill GEMM sweep (configs[2])")
     ap.add_argument("--case", default=None,
@@ -509,6 +584,7 @@ def main():
     gemm = None
     if not args.no_gemm:
         gemm = gemm_sweep(b200, device)
+    sharded = None if args.no_sharded else sharded_bench(b200, world, rank, device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -538,6 +614,7 @@ def main():
             "sweep_w8a16": shapes_w8,
             "sweep_bf16": shapes_bf16,
             "gemm_sweep": gemm,
+            "sharded": sharded,
             "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf_burst,
                       "bf16_tflops_sustained": tf_sust, "kind": peak_kind},
         }

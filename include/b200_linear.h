@@ -133,6 +133,57 @@ int b200_lm_head_w8a16(const int8_t* weight, const uint16_t* scales,
 int b200_argmax_bf16(const uint16_t* values, int n, int* output,
                      b200_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Column-sharded Linear across the GPUs of one node (one process per GPU,
+ * NCCL over NVLink).  The reference is single-GPU; these are the sharded
+ * forms of gemm_w8a16 and lm_head_bf16 (src/cuda/kernels.cu:1566-1579,
+ * 1657-1684) for the large synthetic shapes.  A b200_comm_t wraps an NCCL
+ * communicator whose rank r drives the current CUDA device of its process.
+ * ------------------------------------------------------------------------ */
+typedef struct b200_comm* b200_comm_t;
+
+/* Size of an NCCL unique id (bytes) and a fresh id, made on one rank and
+ * shared with the others out of band (e.g. torch.distributed). */
+int b200_nccl_unique_id_bytes(void);
+int b200_nccl_get_unique_id(void* out);
+
+/* Creates a communicator of nranks (ncclCommInitRank) on the current device. */
+int b200_comm_init(b200_comm_t* comm, const void* unique_id, int nranks,
+                   int rank);
+/* Wraps an existing ncclComm_t (not owned: b200_comm_destroy leaves it). */
+int b200_comm_wrap(b200_comm_t* comm, void* nccl_comm, int nranks, int rank);
+int b200_comm_destroy(b200_comm_t comm);
+
+/* Gather workspace of b200_sharded_gemm_w8a16_allgather: tokens x
+ * out_features BF16 (the [P][tokens][out_features/P] slots). */
+size_t b200_sharded_gemm_workspace_bytes(int tokens, int out_features,
+                                         int nranks);
+
+/* Y[tokens, out_features] = X . W^T + b with W split by rows across ranks:
+ * this rank passes its rows [rank*N/P, (rank+1)*N/P) of W, of the scales and
+ * of the bias; every rank receives the full row-major Y.  out_features must
+ * be a multiple of 8 * nranks.  Enqueues the local tensor-core GEMM, an
+ * NCCL all-gather and a layout copy on `stream`. */
+int b200_sharded_gemm_w8a16_allgather(
+    b200_comm_t comm, const int8_t* weight_shard, const uint16_t* scales_shard,
+    int group_size, const uint16_t* bias_shard, const uint16_t* input,
+    uint16_t* output, void* workspace, int tokens, int out_features,
+    int in_features, b200_stream_t stream);
+
+/* Workspace of b200_sharded_lm_head_bf16 (bytes, 8-byte aligned). */
+size_t b200_sharded_lm_head_workspace_bytes(int vocab, int nranks);
+
+/* Vocabulary-sharded fused LM head: this rank holds vocabulary rows
+ * [rank*V/P, (rank+1)*V/P) and writes their BF16 logits to logits_shard;
+ * every rank receives in *argmax the global index of the largest BF16 logit,
+ * lowest index on ties (one NCCL max all-reduce of a packed 64-bit key).
+ * vocab must be a multiple of nranks. */
+int b200_sharded_lm_head_bf16(b200_comm_t comm, const uint16_t* weight_shard,
+                              const uint16_t* bias_shard,
+                              const uint16_t* input, uint16_t* logits_shard,
+                              void* workspace, int* argmax, int vocab,
+                              int in_features, b200_stream_t stream);
+
 /* Fused LM head that allocates nothing and needs no workspace.
  * No counterpart in the reference (its lm_head_bf16 takes a caller-owned
  * workspace).  For callers that cannot allocate device memory -- a plugin

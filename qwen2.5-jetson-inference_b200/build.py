@@ -21,7 +21,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libb200linear.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu",
+           "sharded.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
               "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
@@ -62,7 +63,8 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=min(4, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra), srcs))
     if _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "shared", "-o", LIB, *objs]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "shared", "-o", LIB, *objs,
+               "-lnccl"]
         subprocess.run(cmd, check=True)
     if verbose:
         print(LIB)

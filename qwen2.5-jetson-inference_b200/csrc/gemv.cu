@@ -460,7 +460,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   constexpr int kWarpRows = kGroups * kR;
   constexpr int kTileRows =
       kWPR > 1 ? kConsumerWarps / kWPR : kConsumerWarps * kWarpRows;
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_bulk[];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -476,7 +476,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   constexpr int kIters = kK != 0 ? (kChunks + kSpan - 1) / kSpan : 0;
   constexpr bool kExact = kK != 0 && kChunks % kSpan == 0;
 
-  float4* xs = reinterpret_cast<float4*>(smem_raw + size_t(stages) * stage_bytes);
+  float4* xs = reinterpret_cast<float4*>(smem_bulk + size_t(stages) * stage_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(xs + (k >> 2));
   const uint32_t bar_full = smem_u32(bars);
   const uint32_t bar_empty = bar_full + 8 * stages;
@@ -511,7 +511,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         const int rows = min(kTileRows, n_rows - row0);
         const uint32_t wbytes = uint32_t(rows) * row_bytes;
         const uint32_t sbytes = kW8 ? uint32_t(rows) * groups * 2 : 0u;
-        unsigned char* st = smem_raw + size_t(s) * stage_bytes;
+        unsigned char* st = smem_bulk + size_t(s) * stage_bytes;
         mbar_arrive_expect_tx(bar_full + 8 * s, wbytes + sbytes);
         bulk_load(smem_u32(st), wbase + size_t(row0) * row_bytes, wbytes,
                   bar_full + 8 * s);
@@ -551,7 +551,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
       if (!mbar_wait_bounded(bar_full + 8 * s, ph, abort_flag,
                              B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status))
         break;
-      const unsigned char* wt = smem_raw + size_t(s) * stage_bytes;
+      const unsigned char* wt = smem_bulk + size_t(s) * stage_bytes;
       const bf16* stile = reinterpret_cast<const bf16*>(wt + w_tile_bytes);
       float2 acc2[kR];
 #pragma unroll

@@ -1,0 +1,276 @@
+// Column-sharded Linear across the GPUs of one node (one process per GPU):
+//
+//  * W8A16 GEMM: rank r owns weight rows (= output columns)
+//    [r*N/P, (r+1)*N/P) and their scales; X is replicated.  The local
+//    tensor-core GEMM writes Y_r [M, N/P] straight into slot r of a gather
+//    buffer [P][M][N/P], an in-place ncclAllGather fills the other slots over
+//    NVLink, and a copy kernel lays the slots out as the row-major [M, N]
+//    output the engine expects.
+//  * LM head: rank r owns vocabulary rows [r*V/P, (r+1)*V/P).  The local
+//    fused GEMV + argmax yields (BF16 logit, global index); it is packed into
+//    a 64-bit key that orders by value and then by lower index,
+//    (orderable(value) << 32) | (0xFFFFFFFF - index), so one
+//    ncclAllReduce(max) over P keys gives the global argmax with the
+//    reference's lowest-index tie rule (src/cuda/kernels.cu:545-603).
+//
+// The reference has no multi-GPU path; these are the sharded forms of its
+// gemm_w8a16 and lm_head_bf16 (src/cuda/kernels.cu:1566-1579, 1657-1684).
+#include <nccl.h>
+
+#include <cfloat>
+#include <climits>
+#include <cstring>
+#include <new>
+
+#include "b200_linear.h"
+#include "common.cuh"
+#include "kernels.h"
+
+struct b200_comm {
+  ncclComm_t nccl = nullptr;
+  int nranks = 1;
+  int rank = 0;
+  bool owned = false;
+};
+
+namespace b200 {
+namespace {
+
+// [P][M][Ns] -> [M][P*Ns], 16 bytes per thread per step.
+__global__ void __launch_bounds__(256)
+gather_to_rows_kernel(const uint4* __restrict__ slots, uint4* __restrict__ out,
+                      int nranks, int m, int ns_vec) {
+  const size_t per_slot = size_t(m) * ns_vec;
+  const size_t total = per_slot * nranks;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const size_t r = i / per_slot;
+    const size_t rem = i - r * per_slot;
+    const size_t row = rem / ns_vec;
+    const size_t c = rem - row * ns_vec;
+    out[row * (size_t(ns_vec) * nranks) + r * ns_vec + c] = slots[i];
+  }
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && v > -FLT_MAX && i < bi);
+}
+
+// Reduces the local per-CTA partials to one packed key with a global index.
+__global__ void __launch_bounds__(1024)
+local_argmax_key_kernel(const float* __restrict__ block_value,
+                        const int* __restrict__ block_index, int count,
+                        int index_offset, unsigned long long* __restrict__ key) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait_primary();
+  float best = -FLT_MAX;
+  int best_index = INT_MAX;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    if (better(block_value[i], block_index[i], best, best_index)) {
+      best = block_value[i];
+      best_index = block_index[i];
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_index, off);
+    if (better(ov, oi, best, best_index)) {
+      best = ov;
+      best_index = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = best_index;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) {
+      if (better(sv[w], si[w], b, bi)) {
+        b = sv[w];
+        bi = si[w];
+      }
+    }
+    // No value above -FLT_MAX on this shard: key 0 loses to every real one
+    // (and decodes to index 0 if all shards are empty, as argmax_bf16 does).
+    unsigned long long k = 0ull;
+    if (bi != INT_MAX) {
+      const unsigned int gi = unsigned(bi + index_offset);
+      k = (static_cast<unsigned long long>(float_order_key(b)) << 32) |
+          (0xFFFFFFFFull - gi);
+    }
+    *key = k;
+  }
+}
+
+__global__ void decode_argmax_key_kernel(const unsigned long long* __restrict__ key,
+                                         int* __restrict__ argmax) {
+  const unsigned long long k = *key;
+  *argmax = k == 0ull ? 0 : int(0xFFFFFFFFull - (k & 0xFFFFFFFFull));
+}
+
+int nccl_status(ncclResult_t r) { return r == ncclSuccess ? B200_OK : B200_ERR_NCCL; }
+
+}  // namespace
+}  // namespace b200
+
+using b200::bf16;
+
+extern "C" {
+
+int b200_nccl_unique_id_bytes(void) { return int(sizeof(ncclUniqueId)); }
+
+int b200_nccl_get_unique_id(void* out) {
+  if (out == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return B200_ERR_NCCL;
+  memcpy(out, &id, sizeof(id));
+  return B200_OK;
+}
+
+int b200_comm_init(b200_comm_t* comm, const void* unique_id, int nranks,
+                   int rank) {
+  if (comm == nullptr || unique_id == nullptr || nranks < 1 || rank < 0 ||
+      rank >= nranks) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  auto* c = new (std::nothrow) b200_comm;
+  if (c == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  if (ncclCommInitRank(&c->nccl, nranks, id, rank) != ncclSuccess) {
+    delete c;
+    return B200_ERR_NCCL;
+  }
+  c->nranks = nranks;
+  c->rank = rank;
+  c->owned = true;
+  *comm = c;
+  return B200_OK;
+}
+
+int b200_comm_wrap(b200_comm_t* comm, void* nccl_comm, int nranks, int rank) {
+  if (comm == nullptr || nccl_comm == nullptr || nranks < 1 || rank < 0 ||
+      rank >= nranks) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  auto* c = new (std::nothrow) b200_comm;
+  if (c == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  c->nccl = static_cast<ncclComm_t>(nccl_comm);
+  c->nranks = nranks;
+  c->rank = rank;
+  c->owned = false;
+  *comm = c;
+  return B200_OK;
+}
+
+int b200_comm_destroy(b200_comm_t comm) {
+  if (comm == nullptr) return B200_OK;
+  int rc = B200_OK;
+  if (comm->owned && comm->nccl != nullptr) {
+    rc = b200::nccl_status(ncclCommDestroy(comm->nccl));
+  }
+  delete comm;
+  return rc;
+}
+
+size_t b200_sharded_gemm_workspace_bytes(int tokens, int out_features,
+                                         int nranks) {
+  if (tokens <= 0 || out_features <= 0 || nranks <= 0) return 0;
+  return size_t(tokens) * size_t(out_features) * 2;
+}
+
+int b200_sharded_gemm_w8a16_allgather(
+    b200_comm_t comm, const int8_t* weight_shard, const uint16_t* scales_shard,
+    int group_size, const uint16_t* bias_shard, const uint16_t* input,
+    uint16_t* output, void* workspace, int tokens, int out_features,
+    int in_features, b200_stream_t stream) {
+  if (group_size != 64) return B200_ERR_GROUP_SIZE;
+  if (comm == nullptr || tokens < 0 || out_features < 0 || in_features <= 0) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  const int p = comm->nranks;
+  if (out_features % p != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int ns = out_features / p;
+  if (tokens == 0 || out_features == 0) return B200_OK;
+  if (ns % 8 != 0) return B200_ERR_INVALID_ARGUMENT;  // 16-byte slot rows
+  if (weight_shard == nullptr || scales_shard == nullptr || input == nullptr ||
+      output == nullptr || workspace == nullptr) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  const size_t slot_elems = size_t(tokens) * ns;
+  bf16* slots = static_cast<bf16*>(workspace);
+  bf16* mine = slots + slot_elems * comm->rank;
+  int rc = b200_gemm_w8a16(weight_shard, scales_shard, 64, bias_shard, input,
+                           reinterpret_cast<uint16_t*>(mine), tokens, ns,
+                           in_features, stream);
+  if (rc != B200_OK) return rc;
+  if (p > 1) {
+    rc = b200::nccl_status(ncclAllGather(mine, slots, slot_elems * 2, ncclUint8,
+                                         comm->nccl, stream));
+    if (rc != B200_OK) return rc;
+  }
+  const int ns_vec = ns / 8;
+  const size_t total = slot_elems * p / 8;
+  int grid = int((total + 255) / 256);
+  if (grid > 148 * 16) grid = 148 * 16;
+  b200::gather_to_rows_kernel<<<grid, 256, 0, stream>>>(
+      reinterpret_cast<const uint4*>(slots), reinterpret_cast<uint4*>(output),
+      p, tokens, ns_vec);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? B200_OK : int(e);
+}
+
+size_t b200_sharded_lm_head_workspace_bytes(int vocab, int nranks) {
+  if (vocab <= 0 || nranks <= 0) return 0;
+  const size_t shard = size_t(vocab) / size_t(nranks);
+  const size_t blocks = (shard + 7) / 8;
+  // 8-byte key first (aligned), then the per-CTA partials.
+  return 8 + blocks * (sizeof(float) + sizeof(int));
+}
+
+int b200_sharded_lm_head_bf16(b200_comm_t comm, const uint16_t* weight_shard,
+                              const uint16_t* bias_shard,
+                              const uint16_t* input, uint16_t* logits_shard,
+                              void* workspace, int* argmax, int vocab,
+                              int in_features, b200_stream_t stream) {
+  if (comm == nullptr || vocab <= 0 || in_features < 0 || argmax == nullptr ||
+      workspace == nullptr || logits_shard == nullptr) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  const int p = comm->nranks;
+  if (vocab % p != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int shard = vocab / p;
+  if (in_features > 0 && (weight_shard == nullptr || input == nullptr)) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  auto* key = static_cast<unsigned long long*>(workspace);
+  float* block_value = reinterpret_cast<float*>(key + 1);
+  const int blocks = (shard + 7) / 8;
+  int* block_index = reinterpret_cast<int*>(block_value + blocks);
+  int grid = 0;
+  cudaError_t e = b200::launch_gemv(
+      false, weight_shard, nullptr, reinterpret_cast<const bf16*>(bias_shard),
+      reinterpret_cast<const bf16*>(input), reinterpret_cast<bf16*>(logits_shard),
+      shard, in_features, block_value, block_index, stream, &grid);
+  if (e != cudaSuccess) return int(e);
+  if (grid > blocks) return B200_ERR_WORKSPACE;
+  b200::local_argmax_key_kernel<<<1, 1024, 0, stream>>>(
+      block_value, block_index, grid, comm->rank * shard, key);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return int(e);
+  if (p > 1) {
+    const int rc = b200::nccl_status(
+        ncclAllReduce(key, key, 1, ncclUint64, ncclMax, comm->nccl, stream));
+    if (rc != B200_OK) return rc;
+  }
+  b200::decode_argmax_key_kernel<<<1, 1, 0, stream>>>(key, argmax);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? B200_OK : int(e);
+}
+
+}  // extern "C"
