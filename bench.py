@@ -538,7 +538,7 @@ def main():
                 traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                 "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
-                "peak_kind": peak_kind, "kernel": "gemv_stream_kernel<W8> 896->151936",
+                "peak_kind": peak_kind, "kernel": "gemv_bulk_kernel<W8> 896->151936",
                 "algorithmic_bytes_per_launch": big["bytes"],
                 "us_per_launch": round(t_big * 1e6, 2)}
     shapes_w8 = per_shape(sweep)
