@@ -10,6 +10,10 @@ Outputs (committed, small):
   exporter_kat.npz   reference tools/export_model.py float32_to_bfloat16 and
                      quantize_groupwise on seeded inputs (group 64, a K=70
                      tail, an all-zero group), i.e. the W8A16 qbin format;
+  qbin_kat.json      archive metadata (dtype/shape/offset/size/SHA-256 of every
+                     tensor) the reference exporter writes for a seeded tiny
+                     Qwen2 in fp32 / w16a16 / w8a16 (weights from
+                     qbin.synthetic_qwen2(TINY_QWEN2, seed=3) with zero groups);
   cpu_linear.npz     reference src/cpu_ops.cpp linear_fp32 / linear_fp32_batch
                      (OpenBLAS FP32) on the deterministic BF16 patterns of the
                      reference's tests/test_cuda.cpp:621-703 (check_bf16_linear_case).
@@ -18,6 +22,7 @@ The tests compare the oracle (oracle/linear_oracle.c) against these.
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import sys
 
@@ -89,7 +94,59 @@ def main():
         out[tag + "_batch"] = y
         out[tag + "_gemv"] = y1
     np.savez_compressed(os.path.join(HERE, "cpu_linear.npz"), **out)
-    print("wrote exporter_kat.npz, cpu_linear.npz")
+    make_qbin_kat(args.reference)
+    print("wrote exporter_kat.npz, cpu_linear.npz, qbin_kat.json")
+
+
+
+TINY_QWEN2 = dict(hidden_size=64, intermediate_size=160, num_hidden_layers=2,
+                  num_attention_heads=4, num_key_value_heads=2, vocab_size=300,
+                  max_position_embeddings=512, rms_norm_eps=1e-6, rope_theta=1000000.0,
+                  tie_word_embeddings=True, bos_token_id=1, eos_token_id=2,
+                  model_type="qwen2")
+
+
+def make_qbin_kat(reference: str):
+    """Archive metadata the reference exporter writes for a seeded tiny Qwen2
+    (every tensor's dtype, shape, offset, size and SHA-256): the writer in
+    qwen2.5-jetson-inference_b200/qbin.py must reproduce it exactly."""
+    import importlib.util
+    import struct
+    import tempfile
+    sys.path.insert(0, os.path.join(reference, "tools"))
+    import export_model as E
+    spec = importlib.util.spec_from_file_location(
+        "qbin", os.path.join(REPO, "qwen2.5-jetson-inference_b200", "qbin.py"))
+    Q = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(Q)
+    tensors = Q.synthetic_qwen2(TINY_QWEN2, seed=3)
+    tensors["model.layers.1.mlp.down_proj.weight"][:, :64] = 0.0  # zero groups
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        src = os.path.join(tmp, "src")
+        os.makedirs(src)
+        header, payload, off = {}, [], 0
+        for name in sorted(tensors):
+            a = np.ascontiguousarray(tensors[name], dtype="<f4")
+            header[name] = {"dtype": "F32", "shape": list(a.shape),
+                            "data_offsets": [off, off + a.nbytes]}
+            payload.append(a)
+            off += a.nbytes
+        enc = json.dumps(header).encode()
+        with open(os.path.join(src, "model.safetensors"), "wb") as f:
+            f.write(struct.pack("<Q", len(enc)))
+            f.write(enc)
+            for a in payload:
+                a.tofile(f)
+        from pathlib import Path
+        for prec in ("fp32", "w16a16", "w8a16"):
+            dst = os.path.join(tmp, f"model.{prec}.qbin")
+            E.export(Path(src), Path(dst), prec, 64)
+            meta = Q.read_records(dst)
+            meta.pop("source")
+            out[prec] = meta
+    with open(os.path.join(HERE, "qbin_kat.json"), "w") as f:
+        json.dump({"config": TINY_QWEN2, "archives": out}, f, indent=0)
 
 
 if __name__ == "__main__":
