@@ -325,6 +325,47 @@ def sharded_bench(b200, world, rank, device, reps=5):
     return out
 
 
+def e2e_bench(new_tokens=128, warmup=2, repeat=5):
+    """the reference engine, unchanged, on the seeded synthetic
+    Qwen2.5-0.5B (24 layers), 32-token uniform prompt, greedy decode without
+    EOS stop, run with the b200 Linear kernels and with the reference's own
+    (custom and cuBLAS), plus the reference CPU FP32 engine on the host cores.
+    Wall-clock TTFT / decode tok/s / TPOT as the reference reports them."""
+    import importlib
+    e2e = importlib.import_module("qwen25_b200.e2e")
+    q = importlib.import_module("qwen25_b200.qbin")
+    try:
+        e2e.binary("b200")
+    except FileNotFoundError as err:
+        return {"unavailable": str(err)}
+    model = e2e.ensure_model("/tmp/b200_e2e_qwen2_05b", dict(q.QWEN25_05B), seed=0)
+    prompt = e2e.prompt_ids(32, seed=0)
+    runs = [("b200", "w8a16", "custom"), ("b200", "w16a16", "custom"),
+            ("reference", "w8a16", "custom"), ("reference", "w16a16", "custom"),
+            ("reference", "w16a16", "cublas")]
+    out = {"prompt_tokens": 32, "new_tokens": new_tokens, "runs": []}
+    tokens = {}
+    for kind, prec, lk in runs:
+        r = e2e.run(kind, model, prompt, precision=prec, linear_kernel=lk,
+                    new_tokens=new_tokens, warmup=warmup, repeat=repeat)
+        tokens[(kind, prec, lk)] = r["tokens"]
+        out["runs"].append({
+            "linear": kind, "precision": prec, "linear_kernel": lk,
+            "decode_tok_s": round(statistics.median(r["decode_tok_s"]), 1),
+            "ttft_ms": round(statistics.median(r["ttft_ms"]), 3),
+            "tpot_ms": round(statistics.median(r["tpot_ms"]), 4)})
+    for prec in ("w8a16", "w16a16"):
+        a, b = tokens[("b200", prec, "custom")], tokens[("reference", prec, "custom")]
+        same = next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
+        out[f"token_identical_prefix_{prec}"] = same
+    cpu = e2e.run("reference", model, prompt, backend="cpu", precision="fp32",
+                  new_tokens=16, warmup=0, repeat=1)
+    out["cpu_fp32"] = {"decode_tok_s": round(cpu["decode_tok_s"][0], 2),
+                       "ttft_ms": round(cpu["ttft_ms"][0], 1), "new_tokens": 16,
+                       "cores": len(os.sched_getaffinity(0))}
+    return out
+
+
 # ------------------------------------------------------------ CPU reference
 def cpu_reference_sample(steps, warmup, budget_s=12.0):
     """Reference src/cpu_ops.cpp linear_fp32 (OpenBLAS sgemv, FP32 weights) on
@@ -471,6 +512,8 @@ def main():
     ap.add_argument("--passes", type=int, default=100, help="sweep passes per step")
     ap.add_argument("--no-gemm", action="store_true", help="skip the GEMM sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end engine runs (configs[3])")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the sharded GEMM / LM head (configs[4])")
     ap.add_argument("--only-gemm", action="store_true",
@@ -585,6 +628,9 @@ def main():
     if not args.no_gemm:
         gemm = gemm_sweep(b200, device)
     sharded = None if args.no_sharded else sharded_bench(b200, world, rank, device)
+    e2e_decode = None
+    if rank == 0 and world == 1 and not args.no_e2e:
+        e2e_decode = e2e_bench()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -615,6 +661,7 @@ def main():
             "sweep_bf16": shapes_bf16,
             "gemm_sweep": gemm,
             "sharded": sharded,
+            "e2e_decode": e2e_decode,
             "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf_burst,
                       "bf16_tflops_sustained": tf_sust, "kind": peak_kind},
         }
