@@ -354,10 +354,24 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
             "decode_tok_s": round(statistics.median(r["decode_tok_s"]), 1),
             "ttft_ms": round(statistics.median(r["ttft_ms"]), 3),
             "tpot_ms": round(statistics.median(r["tpot_ms"]), 4)})
+    def prefix(a, b):
+        return next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
+
     for prec in ("w8a16", "w16a16"):
-        a, b = tokens[("b200", prec, "custom")], tokens[("reference", prec, "custom")]
-        same = next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
-        out[f"token_identical_prefix_{prec}"] = same
+        ref = tokens[("reference", prec, "custom")]
+        out[f"token_identical_prefix_{prec}"] = prefix(tokens[("b200", prec, "custom")], ref)
+        # Teacher-forced: fed the reference kernels' tokens, where do the b200
+        # kernels pick another token, and how close were our top two logits?
+        forced = e2e.run("b200", model, prompt, precision=prec, new_tokens=2, warmup=0,
+                         repeat=1, force_tokens=ref)
+        out[f"teacher_forced_{prec}"] = e2e.forced_agreement(forced, ref)
+    # Control: the reference's own custom kernels against its own cuBLAS path.
+    cub = tokens[("reference", "w16a16", "cublas")]
+    out["reference_custom_vs_cublas_prefix_w16a16"] = prefix(
+        tokens[("reference", "w16a16", "custom")], cub)
+    forced = e2e.run("reference", model, prompt, precision="w16a16", new_tokens=2,
+                     warmup=0, repeat=1, force_tokens=cub)
+    out["reference_custom_vs_cublas_teacher_forced_w16a16"] = e2e.forced_agreement(forced, cub)
     cpu = e2e.run("reference", model, prompt, backend="cpu", precision="fp32",
                   new_tokens=16, warmup=0, repeat=1)
     out["cpu_fp32"] = {"decode_tok_s": round(cpu["decode_tok_s"][0], 2),

@@ -8,12 +8,17 @@
 //              [--precision w16a16|w8a16|fp32] [--linear-kernel custom|cublas]
 //              [--new-tokens 128] [--warmup 5] [--repeat 20]
 //              [--max-seq-len 256] [--logits-out FILE]
+//              [--force-tokens CSV]
 //
 // Output: generated token ids (greedy, no EOS stop, as the reference's
 // benchmark mode runs), per-repeat TTFT / decode tok/s / TPOT (the
 // reference's definitions, include/infer/qwen2.hpp:29-33), and optionally
 // the FP32 logits after prefill (for the cosine check of
-// tests/test_qwen2.cpp:490-511).
+// tests/test_qwen2.cpp:490-511).  With --force-tokens the driver also runs
+// one teacher-forced pass: after the prefill it feeds the given tokens
+// (another engine's greedy output) to decode_next and records its own argmax
+// and the gap between its two largest logits at every step, which tells a
+// near-tie apart from a real disagreement.
 #include <algorithm>
 #include <cstdio>
 #include <fstream>
@@ -85,6 +90,26 @@ int main(int argc, char** argv) {
       f.write(reinterpret_cast<const char*>(logits.data()),
               std::streamsize(logits.size() * sizeof(float)));
     }
+    std::vector<int> forced_argmax;
+    std::vector<float> forced_gap;
+    const auto forced = parse_ids(arg(argc, argv, "--force-tokens"));
+    if (!forced.empty()) {
+      auto gap = [&]() {
+        const auto l = model.last_logits_host();
+        float a = -1e30f, b = -1e30f;
+        for (float v : l) {
+          if (v > a) { b = a; a = v; } else if (v > b) { b = v; }
+        }
+        return a - b;
+      };
+      model.reset();
+      forced_argmax.push_back(model.prefill(prompt));
+      forced_gap.push_back(gap());
+      for (size_t j = 0; j + 1 < forced.size(); ++j) {
+        forced_argmax.push_back(model.decode_next(forced[j]));
+        forced_gap.push_back(gap());
+      }
+    }
     for (int i = 0; i < warmup; ++i) model.generate(prompt, new_tokens, false);
     std::vector<int> tokens;
     std::vector<double> ttft, decode, tpot;
@@ -102,6 +127,8 @@ int main(int argc, char** argv) {
               << ",\"ttft_ms\":" << json_list(ttft)
               << ",\"decode_tok_s\":" << json_list(decode)
               << ",\"tpot_ms\":" << json_list(tpot)
+              << ",\"forced_argmax\":" << json_list(forced_argmax)
+              << ",\"forced_gap\":" << json_list(forced_gap)
               << ",\"device_weight_bytes\":" << model.device_weight_bytes()
               << "}" << std::endl;
   } catch (const std::exception& e) {

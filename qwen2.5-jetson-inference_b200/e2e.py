@@ -52,14 +52,30 @@ def prompt_ids(n: int = 32, vocab: int = 151936, seed: int = 0) -> list[int]:
 def run(kind: str, model_dir: str, prompt: list[int], backend: str = "cuda",
         precision: str = "w16a16", linear_kernel: str = "custom", new_tokens: int = 128,
         warmup: int = 5, repeat: int = 20, max_seq_len: int = 256,
-        logits_out: str | None = None, timeout: int = 1800) -> dict:
+        logits_out: str | None = None, force_tokens: list[int] | None = None,
+        timeout: int = 1800) -> dict:
     cmd = [binary(kind), "--model", model_dir, "--backend", backend, "--precision",
            precision, "--linear-kernel", linear_kernel, "--token-ids",
            ",".join(map(str, prompt)), "--new-tokens", str(new_tokens), "--warmup",
            str(warmup), "--repeat", str(repeat), "--max-seq-len", str(max_seq_len)]
     if logits_out:
         cmd += ["--logits-out", logits_out]
+    if force_tokens:
+        cmd += ["--force-tokens", ",".join(map(str, force_tokens))]
     proc = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
     if proc.returncode != 0:
         raise RuntimeError(f"{' '.join(cmd[:2])} failed: {proc.stderr[-2000:]}")
     return json.loads(proc.stdout.strip().splitlines()[-1])
+
+
+def forced_agreement(ours: dict, reference_tokens: list[int]) -> dict:
+    """Teacher-forced comparison: our argmax at every step when fed the
+    reference engine's tokens.  Disagreements are classified by the gap
+    between our two largest logits, in BF16 ulps of the top logit (the LM head
+    argmax runs on BF16-rounded logits)."""
+    am, gaps = ours["forced_argmax"], ours["forced_gap"]
+    n = min(len(am), len(reference_tokens))
+    dis = [j for j in range(n) if am[j] != reference_tokens[j]]
+    return {"steps": n, "agree": n - len(dis),
+            "disagree_steps": dis,
+            "disagree_gaps": [round(gaps[j], 5) for j in dis]}

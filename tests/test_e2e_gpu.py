@@ -55,3 +55,20 @@ def test_first_token_and_cosine_vs_cpu_fp32(e2e, tmp_path):
     assert cos >= 0.999, cos
     assert ours["tokens"][0] == cpu["tokens"][0] or \
         np.sort(lc)[-1] - np.sort(lc)[-2] < 0.02  # near-tie in FP32
+
+
+@pytest.mark.parametrize("precision", ["w16a16", "w8a16"])
+def test_teacher_forced_disagreements_are_near_ties(e2e, precision):
+    """Fed the reference kernels' tokens, the b200 kernels pick the same next
+    token at every step except where their two largest BF16 logits are within
+    two BF16 ulps (order-of-summation noise decides those)."""
+    prompt = e2e.prompt_ids(32, seed=3)
+    ref = e2e.run("reference", MODEL_DIR, prompt, precision=precision, new_tokens=96,
+                  warmup=0, repeat=1)["tokens"]
+    ours = e2e.run("b200", MODEL_DIR, prompt, precision=precision, new_tokens=2,
+                   warmup=0, repeat=1, force_tokens=ref)
+    res = e2e.forced_agreement(ours, ref)
+    assert res["agree"] >= 0.9 * res["steps"], res
+    top = max(abs(g) for g in ours["forced_gap"]) if ours["forced_gap"] else 0
+    for g in res["disagree_gaps"]:
+        assert g <= 0.0625, res  # <= 2 BF16 ulps for logits in [2, 4)
