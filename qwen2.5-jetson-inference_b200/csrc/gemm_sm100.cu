@@ -467,6 +467,429 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
+// ===================================================================
+// CTA-pair (cta_group::2) GEMM: one 256 x kBN2 output tile per pair of SMs.
+//
+// The two CTAs of a cluster each load 128 rows of X and half (kBN2/2 rows)
+// of the W tile; the leader CTA (rank 0) issues one
+// tcgen05.mma.cta_group::2 (M=256, N=kBN2, K=16) per k step, which reads A
+// from each CTA's own shared memory and B from both halves, and writes each
+// CTA's 128 output rows into that CTA's TMEM.  Per SM this halves the
+// shared-memory traffic of the W operand (loaded once per pair, read once)
+// compared with a one-SM 128 x kBN2 tile -- shared-memory bandwidth
+// (TMA writes + MMA operand reads) is what bounds the one-SM kernel.
+//
+// Synchronisation (barrier offsets are identical in both CTAs):
+//   full[s]   leader; X (and BF16 W) tiles of BOTH CTAs complete_tx here
+//             (the .cta_group::2 TMA form routes the peer's bytes to it);
+//   fullq[s]  each CTA, its raw INT8 W half (W8A16);
+//   dq[s]     leader; 2 x 256 dequant threads arrive (the peer remotely);
+//   empty[s]  each CTA; the leader's tcgen05.commit multicasts to both;
+//   acc_full  each CTA (commit multicast); acc_empty leader, 2 x 128
+//             epilogue threads (the peer remotely).
+// No TMA multicast is used.  All waits are bounded as in the one-SM kernel.
+// ===================================================================
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (arrivals come from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity,
+                                             volatile int* abort_flag, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - start > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      atomicCAS(&g_device_status, 0, code);
+      return false;
+    }
+  }
+}
+// TMA load whose completion is signalled on the leader CTA's barrier.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, int c0,
+                                                 int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::"
+      "complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(bar & 0xFEFFFFFFu)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_commit_both(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster."
+      "multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+template <bool kW8>
+struct Cfg2 {
+  static constexpr int kBN = 256;                 // pair tile N
+  static constexpr int kHalf = kBN / 2;           // W rows per CTA
+  static constexpr int kABytes = 128 * kBK * 2;   // 16 KB
+  static constexpr int kBBytes = kHalf * kBK * 2; // 16 KB (BF16 half tile)
+  static constexpr int kQBytes = kW8 ? kHalf * kBK : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kQBytes;
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 6 ? 6
+                                                              : (200 * 1024) / kStageBytes;
+  static constexpr int kAccCols = kBN;            // fp32 columns per buffer
+  static constexpr int kTmemCols = 2 * kAccCols;  // 512
+  static constexpr int kDqWarps = kW8 ? 8 : 0;
+  static constexpr int kWarps = 8 + kDqWarps;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+};
+
+template <bool kW8>
+__global__ void __launch_bounds__(Cfg2<kW8>::kThreads, 1)
+gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                const __grid_constant__ CUtensorMap tmap_w,
+                const bf16* __restrict__ scales, const bf16* __restrict__ bias,
+                bf16* __restrict__ out, int m, int n, int k) {
+  using C = Cfg2<kW8>;
+  extern __shared__ __align__(1024) unsigned char smem_raw2[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw2) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_fullq = bar_full + 8 * C::kStages;
+  const uint32_t bar_dq = bar_fullq + 8 * C::kStages;
+  const uint32_t bar_empty = bar_dq + 8 * C::kStages;
+  const uint32_t bar_acc_full = bar_empty + 8 * C::kStages;
+  const uint32_t bar_acc_empty = bar_acc_full + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * C::kStages + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_m = (m + 255) / 256;
+  const int num_n = (n + C::kBN - 1) / C::kBN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (k + kBK - 1) / kBK;
+  const int groups = (k + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_fullq + 8 * s, 1);
+      mbar_init(bar_dq + 8 * s, 2 * (C::kDqWarps > 0 ? C::kDqWarps * 32 : 1));
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_acc_full + 8 * a, 1);
+      mbar_init(bar_acc_empty + 8 * a, 2 * 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile(
+        "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+            smem_u32(tmem_slot)),
+        "r"(C::kTmemCols)
+        : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster; tile < num_tiles; tile += num_clusters) {
+        const int mb = tile % num_m;
+        const int nb = tile / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cl(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                            B200_DEVICE_TIMEOUT_PIPELINE))
+            goto producer2_done;
+          unsigned char* st = smem + stage * C::kStageBytes;
+          const uint32_t fb = bar_full + 8 * stage;
+          if (leader) {
+            mbar_arrive_expect_tx(fb, 2 * (C::kABytes + (kW8 ? 0 : C::kBBytes)));
+          }
+          tma_load_2d_pair(smem_u32(st), &tmap_x, kb * kBK, mb * 256 + rank * 128, fb);
+          const int wrow = nb * C::kBN + rank * C::kHalf;
+          if constexpr (kW8) {
+            const uint32_t qb = bar_fullq + 8 * stage;
+            mbar_arrive_expect_tx(qb, C::kQBytes);
+            tma_load_2d(smem_u32(st + C::kABytes + C::kBBytes), &tmap_w, kb * kBK, wrow, qb);
+          } else {
+            tma_load_2d_pair(smem_u32(st + C::kABytes), &tmap_w, kb * kBK, wrow, fb);
+          }
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  producer2_done:;
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(256, C::kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = cluster; tile < num_tiles; tile += num_clusters, ++it) {
+        const int buf = it & 1;
+        const uint32_t use = (it >> 1) & 1;
+        if (!mbar_wait_cl(bar_acc_empty + 8 * buf, use ^ 1, abort_flag,
+                          B200_DEVICE_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t d_base = tmem_base + uint32_t(buf * C::kAccCols);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cl(bar_full + 8 * stage, phase, abort_flag,
+                            B200_DEVICE_TIMEOUT_PIPELINE) ||
+              (kW8 && !mbar_wait_cl(bar_dq + 8 * stage, phase, abort_flag,
+                                    B200_DEVICE_TIMEOUT_PIPELINE))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          unsigned char* st = smem + stage * C::kStageBytes;
+          const uint32_t a_addr = smem_u32(st);
+          const uint32_t b_addr = smem_u32(st + C::kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            mma2_bf16(d_base, desc_sw128(a_addr + kk * 32), desc_sw128(b_addr + kk * 32),
+                      idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma2_commit_both(bar_empty + 8 * stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma2_commit_both(bar_acc_full + 8 * buf);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const bool vec_ok = (n % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+    const uint32_t acc_empty_leader = map_to_rank(bar_acc_empty, 0);
+    int it = 0;
+    for (int tile = cluster; tile < num_tiles; tile += num_clusters, ++it) {
+      const int mb = tile % num_m;
+      const int nb = tile / num_m;
+      const int buf = it & 1;
+      const uint32_t use = (it >> 1) & 1;
+      if (!mbar_wait_cl(bar_acc_full + 8 * buf, use, abort_flag, B200_DEVICE_TIMEOUT_ACCUM))
+        break;
+      tc_fence_after();
+      const int row = mb * 256 + int(rank) * 128 + q * 32 + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < C::kBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * C::kAccCols + c0), r);
+        const int col0 = nb * C::kBN + c0;
+        if (row < m && col0 < n) {
+          bf16* dst = out + size_t(row) * n + col0;
+          if (vec_ok && col0 + 32 <= n) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t packed[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = v * 8 + e * 2;
+                float f0 = __uint_as_float(r[j]);
+                float f1 = __uint_as_float(r[j + 1]);
+                if (bias) {
+                  f0 += __bfloat162float(bias[col0 + j]);
+                  f1 += __bfloat162float(bias[col0 + j + 1]);
+                }
+                const bf162 h = __floats2bfloat162_rn(f0, f1);
+                packed[e] = *reinterpret_cast<const uint32_t*>(&h);
+              }
+              reinterpret_cast<uint4*>(dst)[v] =
+                  make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < n) {
+                float f = __uint_as_float(r[j]);
+                if (bias) f += __bfloat162float(bias[col0 + j]);
+                dst[j] = __float2bfloat16_rn(f);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      if (leader) {
+        mbar_arrive(bar_acc_empty + 8 * buf);
+      } else {
+        mbar_arrive_remote(acc_empty_leader + 8 * buf);
+      }
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------- dequantiser
+    if constexpr (kW8) {
+      const int dt = threadIdx.x - 8 * 32;
+      constexpr int kItems = C::kHalf * 4;
+      constexpr int kPerThread = kItems / (C::kDqWarps * 32);
+      const uint32_t dq_leader = map_to_rank(bar_dq, 0);
+      const uint16_t* sbits = reinterpret_cast<const uint16_t*>(scales);
+      constexpr int kAhead = 4;
+      auto load_scales = [&](int tile, int kb, uint32_t* dst) {
+        const int nb = tile / num_m;
+#pragma unroll
+        for (int p = 0; p < kPerThread; ++p) {
+          const int item = dt + p * (C::kDqWarps * 32);
+          const int row = nb * C::kBN + int(rank) * C::kHalf + (item >> 2);
+          const uint32_t v =
+              (tile < num_tiles && row < n) ? sbits[size_t(row) * groups + kb] : 0u;
+          dst[p] = v | (v << 16);
+        }
+      };
+      int pf_tile = cluster, pf_kb = 0;
+      uint32_t sq[kAhead][kPerThread];
+#pragma unroll
+      for (int d = 0; d < kAhead; ++d) {
+        load_scales(pf_tile, pf_kb, sq[d]);
+        if (++pf_kb == num_kb) {
+          pf_kb = 0;
+          pf_tile += num_clusters;
+        }
+      }
+      const bf162 neg0 = __halves2bfloat162(__ushort_as_bfloat16(0x8000),
+                                            __ushort_as_bfloat16(0x8000));
+      int stage = 0;
+      uint32_t phase = 0;
+      int tile = cluster, kb = 0;
+      while (true) {
+#pragma unroll
+        for (int d = 0; d < kAhead; ++d) {
+          if (tile >= num_tiles) goto dequant2_done;
+          if (!mbar_wait(bar_fullq + 8 * stage, phase, abort_flag,
+                         B200_DEVICE_TIMEOUT_PIPELINE))
+            goto dequant2_done;
+          unsigned char* st = smem + stage * C::kStageBytes;
+          unsigned char* bt = st + C::kABytes;
+          const unsigned char* qt = bt + C::kBBytes;
+#pragma unroll
+          for (int p = 0; p < kPerThread; ++p) {
+            const int item = dt + p * (C::kDqWarps * 32);
+            const int r = item >> 2;
+            const int j = item & 3;
+            const uint4 raw = *reinterpret_cast<const uint4*>(qt + r * kBK + j * 16);
+            const uint32_t s2bits = sq[d][p];
+            const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
+            uint32_t outw[8];
+            const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const uint32_t b = words[wi] ^ 0x80808080u;
+              const uint32_t f0 = __float_as_uint(s8_to_f32_biased<0>(b));
+              const uint32_t f1 = __float_as_uint(s8_to_f32_biased<1>(b));
+              const uint32_t f2 = __float_as_uint(s8_to_f32_biased<2>(b));
+              const uint32_t f3 = __float_as_uint(s8_to_f32_biased<3>(b));
+              uint32_t q01 = __byte_perm(f0, f1, 0x7632);
+              uint32_t q23 = __byte_perm(f2, f3, 0x7632);
+              bf162 d01 = __hfma2(*reinterpret_cast<bf162*>(&q01), s2, neg0);
+              bf162 d23 = __hfma2(*reinterpret_cast<bf162*>(&q23), s2, neg0);
+              outw[2 * wi] = *reinterpret_cast<uint32_t*>(&d01);
+              outw[2 * wi + 1] = *reinterpret_cast<uint32_t*>(&d23);
+            }
+            unsigned char* rowp = bt + (r >> 3) * 1024 + (r & 7) * 128;
+            const int c0 = (2 * j) ^ (r & 7);
+            const int c1 = (2 * j + 1) ^ (r & 7);
+            *reinterpret_cast<uint4*>(rowp + c0 * 16) =
+                make_uint4(outw[0], outw[1], outw[2], outw[3]);
+            *reinterpret_cast<uint4*>(rowp + c1 * 16) =
+                make_uint4(outw[4], outw[5], outw[6], outw[7]);
+          }
+          fence_proxy_async_smem();
+          if (leader) {
+            mbar_arrive(bar_dq + 8 * stage);
+          } else {
+            mbar_arrive_remote(dq_leader + 8 * stage);
+          }
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+          load_scales(pf_tile, pf_kb, sq[d]);
+          if (++pf_kb == num_kb) {
+            pf_kb = 0;
+            pf_tile += num_clusters;
+          }
+          if (++kb == num_kb) {
+            kb = 0;
+            tile += num_clusters;
+          }
+        }
+      }
+    dequant2_done:;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(C::kTmemCols)
+                 : "memory");
+  }
+}
+
 // ------------------------------------------------------------------- host
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -536,6 +959,46 @@ cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
   return cudaGetLastError();
 }
 
+template <bool kW8>
+cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias,
+                        const bf16* input, bf16* output, int m, int n, int k,
+                        cudaStream_t stream) {
+  using C = Cfg2<kW8>;
+  CUtensorMap tx, tw;
+  if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (kW8) {
+    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, C::kHalf,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK, C::kHalf,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  }
+  auto kernel = gemm_tc2_kernel<kW8>;
+  cudaError_t e = cudaFuncSetAttribute(
+      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int tiles = ((m + 255) / 256) * ((n + C::kBN - 1) / C::kBN);
+  const int pairs = sm_count() / 2;
+  const int clusters = tiles < pairs ? tiles : pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k);
+}
+
 bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
@@ -543,7 +1006,7 @@ bool aligned16(const void* p) {
 
 // Tile-shape choice: the largest tile that still gives every SM work.
 // B200_GEMM_TILE=256x128|128x256|128x128|128x64 overrides it (tuning only).
-enum class Tile { k256x128, k128x256, k128x128, k128x64 };
+enum class Tile { kPair256x256, k256x128, k128x256, k128x128, k128x64 };
 
 // BF16 prefers 128x256 (one N=256 MMA per k-step reads less shared memory
 // per FLOP than two M=128 x N=128 MMAs); INT8 weights prefer 256x128, which
@@ -551,6 +1014,7 @@ enum class Tile { k256x128, k128x256, k128x128, k128x64 };
 Tile choose_tile(bool w8, int m, int n) {
   static const char* forced = getenv("B200_GEMM_TILE");
   if (forced) {
+    if (!strcmp(forced, "pair")) return Tile::kPair256x256;
     if (!strcmp(forced, "256x128")) return Tile::k256x128;
     if (!strcmp(forced, "128x256")) return Tile::k128x256;
     if (!strcmp(forced, "128x128")) return Tile::k128x128;
@@ -571,6 +1035,8 @@ cudaError_t launch_tile(Tile t, const void* weight, const bf16* scales,
                         const bf16* bias, const bf16* input, bf16* output,
                         int m, int n, int k, cudaStream_t stream) {
   switch (t) {
+    case Tile::kPair256x256:
+      return launch_pair<kW8>(weight, scales, bias, input, output, m, n, k, stream);
     case Tile::k256x128:
       return launch_cfg<kW8, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
     case Tile::k128x256:
