@@ -483,10 +483,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 //   full[s]   leader; X (and BF16 W) tiles of BOTH CTAs complete_tx here
 //             (the .cta_group::2 TMA form routes the peer's bytes to it);
 //   fullq[s]  each CTA, its raw INT8 W half (W8A16);
-//   dq[s]     leader; 2 x 256 dequant threads arrive (the peer remotely);
+//   dq[s]     leader; one arrival per CTA after its dequant threads meet
+//             on a named barrier (the peer's arrival is remote);
 //   empty[s]  each CTA; the leader's tcgen05.commit multicasts to both;
-//   acc_full  each CTA (commit multicast); acc_empty leader, 2 x 128
-//             epilogue threads (the peer remotely).
+//   acc_full  each CTA (commit multicast); acc_empty leader, one arrival
+//             per CTA after its four epilogue warps meet.
 // No TMA multicast is used.  All waits are bounded as in the one-SM kernel.
 // ===================================================================
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -615,12 +616,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_fullq + 8 * s, 1);
-      mbar_init(bar_dq + 8 * s, 2 * (C::kDqWarps > 0 ? C::kDqWarps * 32 : 1));
+      mbar_init(bar_dq + 8 * s, 2);  // one arrival per CTA
       mbar_init(bar_empty + 8 * s, 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_acc_full + 8 * a, 1);
-      mbar_init(bar_acc_empty + 8 * a, 2 * 128);
+      mbar_init(bar_acc_empty + 8 * a, 2);  // one arrival per CTA
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -770,10 +771,15 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
         }
       }
       tc_fence_before();
-      if (leader) {
-        mbar_arrive(bar_acc_empty + 8 * buf);
-      } else {
-        mbar_arrive_remote(acc_empty_leader + 8 * buf);
+      // The four epilogue warps meet first, so one arrival per CTA (a remote
+      // one from the peer) releases the accumulator.
+      asm volatile("bar.sync 3, 128;" ::: "memory");
+      if (threadIdx.x == 4 * 32) {
+        if (leader) {
+          mbar_arrive(bar_acc_empty + 8 * buf);
+        } else {
+          mbar_arrive_remote(acc_empty_leader + 8 * buf);
+        }
       }
     }
   } else if (warp >= 8) {
@@ -854,10 +860,14 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 make_uint4(outw[4], outw[5], outw[6], outw[7]);
           }
           fence_proxy_async_smem();
-          if (leader) {
-            mbar_arrive(bar_dq + 8 * stage);
-          } else {
-            mbar_arrive_remote(dq_leader + 8 * stage);
+          // All dequant threads of this CTA meet, then one arrival per CTA.
+          asm volatile("bar.sync 2, %0;" ::"r"(C::kDqWarps * 32) : "memory");
+          if (dt == 0) {
+            if (leader) {
+              mbar_arrive(bar_dq + 8 * stage);
+            } else {
+              mbar_arrive_remote(dq_leader + 8 * stage);
+            }
           }
           if (++stage == C::kStages) {
             stage = 0;
