@@ -483,9 +483,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 //   full[s]   leader; X (and BF16 W) tiles of BOTH CTAs complete_tx here
 //             (the .cta_group::2 TMA form routes the peer's bytes to it);
 //   fullq[s]  each CTA, its raw INT8 W half (W8A16);
-//   dq[s]     leader; one arrival per CTA after its dequant threads meet
-//             on a named barrier (the peer's arrival is remote);
 //   empty[s]  each CTA; the leader's tcgen05.commit multicasts to both;
+//   W8A16 only: the dequantised W halves live in a separate 3-slot ring,
+//   dq[d]     leader; one arrival per CTA after its dequant threads meet
+//             on a named barrier (the peer's arrival is remote);
+//   dq_empty[d] each CTA (commit multicast) -- so the TMA ring of X and raw
+//             INT8 tiles can run 6 stages ahead of the dequant hand-off;
 //   acc_full  each CTA (commit multicast); acc_empty leader, one arrival
 //             per CTA after its four epilogue warps meet.
 // No TMA multicast is used.  All waits are bounded as in the one-SM kernel.
@@ -569,15 +572,22 @@ struct Cfg2 {
   static constexpr int kABytes = 128 * kBK * 2;   // 16 KB
   static constexpr int kBBytes = kHalf * kBK * 2; // 16 KB (BF16 half tile)
   static constexpr int kQBytes = kW8 ? kHalf * kBK : 0;
-  static constexpr int kStageBytes = kABytes + kBBytes + kQBytes;
-  static constexpr int kStages = (200 * 1024) / kStageBytes > 6 ? 6
-                                                              : (200 * 1024) / kStageBytes;
+  // Raw ring (TMA destination): X half + (BF16 W half | raw INT8 W half).
+  static constexpr int kStageBytes = kABytes + (kW8 ? kQBytes : kBBytes);
+  // INT8: a separate, shorter ring of dequantised W halves, so the TMA ring
+  // runs deep ahead of the dequant -> MMA hand-off.
+  static constexpr int kDqStages = kW8 ? 3 : 0;
+  static constexpr int kDqBytes = kW8 ? kBBytes : 0;
+  static constexpr int kRingBudget = 196 * 1024 - kDqStages * kDqBytes;
+  static constexpr int kStages = kRingBudget / kStageBytes > 6 ? 6
+                                                               : kRingBudget / kStageBytes;
   static constexpr int kAccCols = kBN;            // fp32 columns per buffer
   static constexpr int kTmemCols = 2 * kAccCols;  // 512
   static constexpr int kDqWarps = kW8 ? 8 : 0;
   static constexpr int kWarps = 8 + kDqWarps;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kDqStages * kDqBytes + 512 + 1024;
 };
 
 template <bool kW8>
@@ -590,14 +600,17 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
   extern __shared__ __align__(1024) unsigned char smem_raw2[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw2) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  unsigned char* dq_ring = smem + C::kStages * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dq_ring + C::kDqStages * C::kDqBytes);
   const uint32_t bar_full = smem_u32(bars);
   const uint32_t bar_fullq = bar_full + 8 * C::kStages;
-  const uint32_t bar_dq = bar_fullq + 8 * C::kStages;
-  const uint32_t bar_empty = bar_dq + 8 * C::kStages;
-  const uint32_t bar_acc_full = bar_empty + 8 * C::kStages;
+  const uint32_t bar_empty = bar_fullq + 8 * C::kStages;
+  const uint32_t bar_dq = bar_empty + 8 * C::kStages;          // [kDqStages]
+  const uint32_t bar_dq_empty = bar_dq + 8 * C::kDqStages;     // [kDqStages]
+  const uint32_t bar_acc_full = bar_dq_empty + 8 * C::kDqStages;
   const uint32_t bar_acc_empty = bar_acc_full + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * C::kStages + 4);
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(bars + 3 * C::kStages + 2 * C::kDqStages + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -616,8 +629,11 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_fullq + 8 * s, 1);
-      mbar_init(bar_dq + 8 * s, 2);  // one arrival per CTA
       mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int d = 0; d < C::kDqStages; ++d) {
+      mbar_init(bar_dq + 8 * d, 2);        // one arrival per CTA
+      mbar_init(bar_dq_empty + 8 * d, 1);  // leader's commit multicast
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_acc_full + 8 * a, 1);
@@ -662,7 +678,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
           if constexpr (kW8) {
             const uint32_t qb = bar_fullq + 8 * stage;
             mbar_arrive_expect_tx(qb, C::kQBytes);
-            tma_load_2d(smem_u32(st + C::kABytes + C::kBBytes), &tmap_w, kb * kBK, wrow, qb);
+            tma_load_2d(smem_u32(st + C::kABytes), &tmap_w, kb * kBK, wrow, qb);
           } else {
             tma_load_2d_pair(smem_u32(st + C::kABytes), &tmap_w, kb * kBK, wrow, fb);
           }
@@ -680,6 +696,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
       constexpr uint32_t idesc = idesc_bf16(256, C::kBN);
       int stage = 0;
       uint32_t phase = 0;
+      int dstage = 0;
+      uint32_t dphase = 0;
       int it = 0;
       for (int tile = cluster; tile < num_tiles; tile += num_clusters, ++it) {
         const int buf = it & 1;
@@ -693,7 +711,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cl(bar_full + 8 * stage, phase, abort_flag,
                             B200_DEVICE_TIMEOUT_PIPELINE) ||
-              (kW8 && !mbar_wait_cl(bar_dq + 8 * stage, phase, abort_flag,
+              (kW8 && !mbar_wait_cl(bar_dq + 8 * dstage, dphase, abort_flag,
                                     B200_DEVICE_TIMEOUT_PIPELINE))) {
             ok = false;
             break;
@@ -701,7 +719,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
           tc_fence_after();
           unsigned char* st = smem + stage * C::kStageBytes;
           const uint32_t a_addr = smem_u32(st);
-          const uint32_t b_addr = smem_u32(st + C::kABytes);
+          const uint32_t b_addr =
+              kW8 ? smem_u32(dq_ring + dstage * C::kDqBytes) : smem_u32(st + C::kABytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             mma2_bf16(d_base, desc_sw128(a_addr + kk * 32), desc_sw128(b_addr + kk * 32),
@@ -711,6 +730,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
+          }
+          if constexpr (kW8) {
+            mma2_commit_both(bar_dq_empty + 8 * dstage);
+            if (++dstage == C::kDqStages) {
+              dstage = 0;
+              dphase ^= 1;
+            }
           }
         }
         if (!ok) break;
@@ -816,17 +842,21 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                             __ushort_as_bfloat16(0x8000));
       int stage = 0;
       uint32_t phase = 0;
+      int dstage = 0;
+      uint32_t dphase = 0;
       int tile = cluster, kb = 0;
       while (true) {
 #pragma unroll
         for (int d = 0; d < kAhead; ++d) {
           if (tile >= num_tiles) goto dequant2_done;
           if (!mbar_wait(bar_fullq + 8 * stage, phase, abort_flag,
-                         B200_DEVICE_TIMEOUT_PIPELINE))
+                         B200_DEVICE_TIMEOUT_PIPELINE) ||
+              !mbar_wait_cl(bar_dq_empty + 8 * dstage, dphase ^ 1, abort_flag,
+                            B200_DEVICE_TIMEOUT_PIPELINE))
             goto dequant2_done;
           unsigned char* st = smem + stage * C::kStageBytes;
-          unsigned char* bt = st + C::kABytes;
-          const unsigned char* qt = bt + C::kBBytes;
+          unsigned char* bt = dq_ring + dstage * C::kDqBytes;
+          const unsigned char* qt = st + C::kABytes;
 #pragma unroll
           for (int p = 0; p < kPerThread; ++p) {
             const int item = dt + p * (C::kDqWarps * 32);
@@ -864,14 +894,18 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
           asm volatile("bar.sync 2, %0;" ::"r"(C::kDqWarps * 32) : "memory");
           if (dt == 0) {
             if (leader) {
-              mbar_arrive(bar_dq + 8 * stage);
+              mbar_arrive(bar_dq + 8 * dstage);
             } else {
-              mbar_arrive_remote(dq_leader + 8 * stage);
+              mbar_arrive_remote(dq_leader + 8 * dstage);
             }
           }
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
+          }
+          if (++dstage == C::kDqStages) {
+            dstage = 0;
+            dphase ^= 1;
           }
           load_scales(pf_tile, pf_kb, sq[d]);
           if (++pf_kb == num_kb) {
