@@ -299,9 +299,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const int nb = tile / num_m;
       const int buf = C::kAccBufs == 2 ? (it & 1) : 0;
       const uint32_t use = C::kAccBufs == 2 ? ((it >> 1) & 1) : (it & 1);
-      if (!mbar_wait(bar_acc_full + 8 * buf, use, abort_flag,
-                     B200_DEVICE_TIMEOUT_ACCUM))
-        break;
+      // Warp-uniform decision: tcgen05.ld needs every lane of the warp.
+      const bool acc_ok = mbar_wait(bar_acc_full + 8 * buf, use, abort_flag,
+                                    B200_DEVICE_TIMEOUT_ACCUM);
+      if (!__all_sync(0xffffffffu, acc_ok)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int s = 0; s < kMSub; ++s) {
@@ -754,12 +755,18 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const int nb = tile / num_m;
       const int buf = it & 1;
       const uint32_t use = (it >> 1) & 1;
-      if (!mbar_wait_cl(bar_acc_full + 8 * buf, use, abort_flag, B200_DEVICE_TIMEOUT_ACCUM))
-        break;
+      // A failed wait does not leave the loop: every epilogue thread must
+      // still meet the others at the named barrier below (a thread that left
+      // would strand them); once the abort flag is up the remaining waits
+      // fail at once and the work is skipped.  The decision is warp-uniform
+      // because tcgen05.ld needs every lane of the warp.
+      const bool acc_ok = __all_sync(
+          0xffffffffu,
+          mbar_wait_cl(bar_acc_full + 8 * buf, use, abort_flag, B200_DEVICE_TIMEOUT_ACCUM));
       tc_fence_after();
       const int row = mb * 256 + int(rank) * 128 + q * 32 + lane;
 #pragma unroll 1
-      for (int c0 = 0; c0 < C::kBN; c0 += 32) {
+      for (int c0 = 0; acc_ok && c0 < C::kBN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * C::kAccCols + c0), r);
         const int col0 = nb * C::kBN + c0;
@@ -849,16 +856,18 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
 #pragma unroll
         for (int d = 0; d < kAhead; ++d) {
           if (tile >= num_tiles) goto dequant2_done;
-          if (!mbar_wait(bar_fullq + 8 * stage, phase, abort_flag,
-                         B200_DEVICE_TIMEOUT_PIPELINE) ||
-              !mbar_wait_cl(bar_dq_empty + 8 * dstage, dphase ^ 1, abort_flag,
-                            B200_DEVICE_TIMEOUT_PIPELINE))
-            goto dequant2_done;
+          // As in the epilogue, a failed wait skips the work but keeps the
+          // thread in step with the named barrier below.
+          const bool ok = mbar_wait(bar_fullq + 8 * stage, phase, abort_flag,
+                                    B200_DEVICE_TIMEOUT_PIPELINE) &&
+                          mbar_wait_cl(bar_dq_empty + 8 * dstage, dphase ^ 1, abort_flag,
+                                       B200_DEVICE_TIMEOUT_PIPELINE);
           unsigned char* st = smem + stage * C::kStageBytes;
           unsigned char* bt = dq_ring + dstage * C::kDqBytes;
           const unsigned char* qt = st + C::kABytes;
 #pragma unroll
           for (int p = 0; p < kPerThread; ++p) {
+            if (!ok) break;
             const int item = dt + p * (C::kDqWarps * 32);
             const int r = item >> 2;
             const int j = item & 3;
@@ -1049,12 +1058,14 @@ bool aligned16(const void* p) {
 
 
 // Tile-shape choice: the largest tile that still gives every SM work.
-// B200_GEMM_TILE=256x128|128x256|128x128|128x64 overrides it (tuning only).
+// B200_GEMM_TILE=pair|256x128|128x256|128x128|128x64 overrides it (tuning only).
 enum class Tile { kPair256x256, k256x128, k128x256, k128x128, k128x64 };
 
-// BF16 prefers 128x256 (one N=256 MMA per k-step reads less shared memory
-// per FLOP than two M=128 x N=128 MMAs); INT8 weights prefer 256x128, which
-// dequantises each weight tile once for 256 token rows.
+// BF16 prefers the CTA-pair 256x256 tile, then 128x256 (one N=256 MMA per
+// k-step reads less shared memory per FLOP than two M=128 x N=128 MMAs);
+// INT8 weights prefer 256x128, which dequantises each weight tile once for
+// 256 token rows (the pair kernel's INT8 form measured slower: the
+// dequant-to-MMA hand-off across the two SMs limits it).
 Tile choose_tile(bool w8, int m, int n) {
   static const char* forced = getenv("B200_GEMM_TILE");
   if (forced) {
@@ -1068,6 +1079,8 @@ Tile choose_tile(bool w8, int m, int n) {
   const long long t256x128 = ((m + 255) / 256) * (long long)((n + 127) / 128);
   const long long t128x128 = ((m + 127) / 128) * (long long)((n + 127) / 128);
   const long long t128x256 = ((m + 127) / 128) * (long long)((n + 255) / 256);
+  const long long tpair = ((m + 255) / 256) * (long long)((n + 255) / 256);
+  if (!w8 && tpair >= sms / 2) return Tile::kPair256x256;
   if (!w8 && t128x256 >= sms) return Tile::k128x256;
   if (t256x128 >= sms) return Tile::k256x128;
   if (t128x128 >= sms / 2) return Tile::k128x128;

@@ -548,9 +548,14 @@ gemv_bulk_kernel(const void* __restrict__ weight,
     for (int tile = blockIdx.x; tile < num_tiles;
          tile += gridDim.x, ++i, s = (s + 1 == stages ? 0 : s + 1),
              ph ^= (s == 0 ? 1u : 0u)) {
-      if (!mbar_wait_bounded(bar_full + 8 * s, ph, abort_flag,
-                             B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status))
-        break;
+      // Warp-uniform outcome.  Split rows (kWPR > 1) meet at a named barrier
+      // every tile, so a failed wait must not make a warp leave the loop
+      // early: it skips the work instead (later waits fail at once once the
+      // abort flag is up).
+      const bool ok = __all_sync(
+          0xffffffffu, mbar_wait_bounded(bar_full + 8 * s, ph, abort_flag,
+                                         B200_DEVICE_TIMEOUT_PIPELINE, &g_gemv_status));
+      if (!ok && kWPR == 1) break;
       const unsigned char* wt = smem_bulk + size_t(s) * stage_bytes;
       const bf16* stile = reinterpret_cast<const bf16*>(wt + w_tile_bytes);
       float2 acc2[kR];
@@ -583,12 +588,12 @@ gemv_bulk_kernel(const void* __restrict__ weight,
           }
         }
       };
-      const int c0 = ksub * kLPR + ll;
+      const int c0 = ok ? ksub * kLPR + ll : chunks;  // failed: no chunks
       if constexpr (kK != 0) {
 #pragma unroll
         for (int j = 0; j < kIters; ++j) {
           const int c = c0 + j * kSpan;
-          if (kExact || c < kChunks) chunk_step(c);
+          if ((kExact && ok) || c < kChunks) chunk_step(c);
         }
       } else {
 #pragma unroll 2
@@ -617,7 +622,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
           }
         }
         const int row = row0 + r;
-        if (ll == 0 && ksub == 0 && row < n_rows) {
+        if (ok && ll == 0 && ksub == 0 && row < n_rows) {
           const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
           const bf16 y = __float2bfloat16_rn(v + b);
           output[row] = y;
