@@ -4,10 +4,12 @@
  * Drop-in boundary for the reference engine's CUDA Linear interface
  * (reference include/infer/cuda_ops.hpp:24-55,102-103; implemented there in
  * src/cuda/kernels.cu:1540-1704).  Every entry point takes raw device
- * pointers, sizes and a CUDA stream; nothing here allocates device memory,
- * synchronises the stream, or keeps state between calls (except the
- * device-side error word read by b200_device_status and the fixed scratch
- * array of b200_lm_head_bf16_noalloc).  All work is enqueued
+ * pointers, sizes and a CUDA stream; nothing here synchronises the stream
+ * or keeps state between calls, except the device-side error word read by
+ * b200_device_status, the fixed scratch array of b200_lm_head_bf16_noalloc,
+ * and the BF16 weight buffer of the two-pass W8A16 prefill (allocated once
+ * per device by b200_gemm_reserve_scratch or by the first large W8A16 GEMM;
+ * no other call allocates device memory).  All work is enqueued
  * asynchronously on `stream`, exactly like the reference functions.
  *
  * Layouts (reference conventions, src/qwen2.cpp:231-330):
@@ -99,6 +101,17 @@ int b200_gemm_w8a16(const int8_t* weight, const uint16_t* scales,
                     int group_size, const uint16_t* bias,
                     const uint16_t* input, uint16_t* output, int tokens,
                     int out_features, int in_features, b200_stream_t stream);
+
+/* Allocates now, on the current device, the BF16 weight buffer (at most
+ * 256 MiB, or `bytes` if smaller and non-zero) that b200_gemm_w8a16 uses for
+ * prefills of >= 1024 tokens: the INT8 weights are dequantised once to
+ * bf16(q*s) and the tensor-core BF16 GEMM runs on them (same results as the
+ * one-pass kernel).  Without this call the buffer is allocated by the first
+ * such GEMM that is not being captured into a CUDA graph; while it is absent
+ * the one-pass kernel runs.  Call it before capturing graphs.  No reference
+ * counterpart (the reference allocates its prefill workspace at start-up,
+ * src/qwen2.cpp:80-200). */
+int b200_gemm_reserve_scratch(size_t bytes);
 
 /* Bytes of workspace b200_lm_head_* need, split as the reference splits it:
  * ceil(vocab/8) floats followed by ceil(vocab/8) ints

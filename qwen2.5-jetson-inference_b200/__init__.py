@@ -42,6 +42,7 @@ _SIGNATURES = {
     "b200_lm_head_bf16": ([_p, _p, _p, _p, _p, _p, _p, _i, _i, _p], _i),
     "b200_lm_head_w8a16": ([_p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p], _i),
     "b200_argmax_bf16": ([_p, _i, _p, _p], _i),
+    "b200_gemm_reserve_scratch": ([ctypes.c_size_t], _i),
     "b200_lm_head_noalloc_max_vocab": ([], ctypes.c_size_t),
     "b200_lm_head_bf16_noalloc": ([_p, _p, _p, _p, _p, _i, _i, _p], _i),
 }

@@ -155,6 +155,10 @@ int b200_gemv_w8a16(const int8_t* weight, const uint16_t* scales,
                                      nullptr));
 }
 
+int b200_gemm_reserve_scratch(size_t bytes) {
+  return status_of(b200::reserve_gemm_scratch(bytes));
+}
+
 int b200_gemm_bf16(const uint16_t* weight, const uint16_t* bias,
                    const uint16_t* input, uint16_t* output, int tokens,
                    int out_features, int in_features, b200_stream_t stream) {

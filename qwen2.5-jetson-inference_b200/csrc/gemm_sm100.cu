@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(Cfg<kW8, kMSub, kBN>::kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_w,
                const bf16* __restrict__ scales, const bf16* __restrict__ bias,
-               bf16* __restrict__ out, int m, int n, int k) {
+               bf16* __restrict__ out, int m, int n, int k, int ldc) {
   using C = Cfg<kW8, kMSub, kBN>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -292,7 +292,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter
     const bool vec_ok =
-        (n % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+        (ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int mb = tile % num_m;
@@ -315,7 +315,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     r);
           const int col0 = nb * kBN + c0;
           if (row < m && col0 < n) {
-            bf16* dst = out + size_t(row) * n + col0;
+            bf16* dst = out + size_t(row) * ldc + col0;
             if (vec_ok && col0 + 32 <= n) {
 #pragma unroll
               for (int v = 0; v < 4; ++v) {
@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(Cfg2<kW8>::kThreads, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
                 const bf16* __restrict__ scales, const bf16* __restrict__ bias,
-                bf16* __restrict__ out, int m, int n, int k) {
+                bf16* __restrict__ out, int m, int n, int k, int ldc) {
   using C = Cfg2<kW8>;
   extern __shared__ __align__(1024) unsigned char smem_raw2[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -747,7 +747,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const bool vec_ok = (n % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+    const bool vec_ok = (ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
     const uint32_t acc_empty_leader = map_to_rank(bar_acc_empty, 0);
     int it = 0;
     for (int tile = cluster; tile < num_tiles; tile += num_clusters, ++it) {
@@ -771,7 +771,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
         tmem_ld32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * C::kAccCols + c0), r);
         const int col0 = nb * C::kBN + c0;
         if (row < m && col0 < n) {
-          bf16* dst = out + size_t(row) * n + col0;
+          bf16* dst = out + size_t(row) * ldc + col0;
           if (vec_ok && col0 + 32 <= n) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -986,7 +986,7 @@ int sm_count() {
 template <bool kW8, int kMSub, int kBN>
 cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
                        const bf16* input, bf16* output, int m, int n, int k,
-                       cudaStream_t stream) {
+                       int ldc, cudaStream_t stream) {
   using C = Cfg<kW8, kMSub, kBN>;
   CUtensorMap tx, tw;
   if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
@@ -1008,14 +1008,14 @@ cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
   const int tiles = ((m + C::kBM - 1) / C::kBM) * ((n + kBN - 1) / kBN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, scales, bias,
-                                                        output, m, n, k);
+                                                        output, m, n, k, ldc);
   return cudaGetLastError();
 }
 
 template <bool kW8>
 cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias,
                         const bf16* input, bf16* output, int m, int n, int k,
-                        cudaStream_t stream) {
+                        int ldc, cudaStream_t stream) {
   using C = Cfg2<kW8>;
   CUtensorMap tx, tw;
   if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
@@ -1049,7 +1049,7 @@ cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k);
+  return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k, ldc);
 }
 
 bool aligned16(const void* p) {
@@ -1090,18 +1090,18 @@ Tile choose_tile(bool w8, int m, int n) {
 template <bool kW8>
 cudaError_t launch_tile(Tile t, const void* weight, const bf16* scales,
                         const bf16* bias, const bf16* input, bf16* output,
-                        int m, int n, int k, cudaStream_t stream) {
+                        int m, int n, int k, int ldc, cudaStream_t stream) {
   switch (t) {
     case Tile::kPair256x256:
-      return launch_pair<kW8>(weight, scales, bias, input, output, m, n, k, stream);
+      return launch_pair<kW8>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     case Tile::k256x128:
-      return launch_cfg<kW8, 2, 128>(weight, scales, bias, input, output, m, n, k, stream);
+      return launch_cfg<kW8, 2, 128>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     case Tile::k128x256:
-      return launch_cfg<kW8, 1, 256>(weight, scales, bias, input, output, m, n, k, stream);
+      return launch_cfg<kW8, 1, 256>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     case Tile::k128x128:
-      return launch_cfg<kW8, 1, 128>(weight, scales, bias, input, output, m, n, k, stream);
+      return launch_cfg<kW8, 1, 128>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     default:
-      return launch_cfg<kW8, 1, 64>(weight, scales, bias, input, output, m, n, k, stream);
+      return launch_cfg<kW8, 1, 64>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }
 }
 
@@ -1116,12 +1116,138 @@ bool gemm_tc_supported(bool w8, const void* weight, const void* input,
   return get_encode_fn() != nullptr;
 }
 
+// ---------------------------------------------------------------------------
+// Two-pass W8A16 prefill for many tokens: the INT8 weights are dequantised
+// once into BF16 -- bf16(q * s), the exact value the in-kernel dequant feeds
+// the MMA -- and the CTA-pair BF16 GEMM runs on them.  At M >= 1024 the extra
+// pass over W (1 byte read + 2 written per weight) costs a few percent of
+// the GEMM, while the in-kernel hand-off of dequantised tiles to the tensor
+// cores limits the one-pass kernel to about half the BF16 rate.  The BF16
+// weights go to a device buffer owned by the library (one per device,
+// kScratchCap bytes at most; W is processed in row blocks that fit).  The
+// buffer is allocated by b200_gemm_reserve_scratch, or by the first such GEMM
+// on a device that is not being captured into a CUDA graph; when it is not
+// available the one-pass kernel runs instead (same results).
+namespace {
+
+constexpr size_t kScratchCap = size_t(256) << 20;
+constexpr int kTwoPassMinTokens = 1024;
+
+struct Scratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_scratch_mutex;
+Scratch g_scratch[64];
+
+cudaError_t scratch_get(size_t want, bool may_allocate, Scratch* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  Scratch& sc = g_scratch[dev];
+  if (sc.ptr == nullptr && may_allocate) {
+    const size_t bytes = want < kScratchCap ? want : kScratchCap;
+    e = cudaMalloc(&sc.ptr, bytes);
+    if (e != cudaSuccess) {
+      sc.ptr = nullptr;
+      cudaGetLastError();
+      return e;
+    }
+    sc.bytes = bytes;
+  }
+  *out = sc;
+  return sc.ptr != nullptr ? cudaSuccess : cudaErrorMemoryAllocation;
+}
+
+// rows x k INT8 + BF16 group-64 scales -> rows x k BF16, 16 weights per thread.
+__global__ void __launch_bounds__(256)
+dequant_w8_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ scales,
+                  int groups, bf16* __restrict__ out, int rows, int k) {
+  const int cpr = k >> 4;  // 16-byte chunks per row
+  const size_t total = size_t(rows) * cpr;
+  const bf162 neg0 = __halves2bfloat162(__ushort_as_bfloat16(0x8000),
+                                        __ushort_as_bfloat16(0x8000));
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const size_t row = i / cpr;
+    const int c = int(i - row * cpr);
+    const uint4 raw = reinterpret_cast<const uint4*>(q)[i];
+    const uint32_t sv = scales[row * groups + (c >> 2)];
+    const uint32_t s2bits = sv | (sv << 16);
+    const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
+    uint32_t w[8];
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+      const uint32_t b = words[wi] ^ 0x80808080u;
+      const uint32_t f0 = __float_as_uint(s8_to_f32_biased<0>(b));
+      const uint32_t f1 = __float_as_uint(s8_to_f32_biased<1>(b));
+      const uint32_t f2 = __float_as_uint(s8_to_f32_biased<2>(b));
+      const uint32_t f3 = __float_as_uint(s8_to_f32_biased<3>(b));
+      uint32_t q01 = __byte_perm(f0, f1, 0x7632);
+      uint32_t q23 = __byte_perm(f2, f3, 0x7632);
+      bf162 d01 = __hfma2(*reinterpret_cast<bf162*>(&q01), s2, neg0);
+      bf162 d23 = __hfma2(*reinterpret_cast<bf162*>(&q23), s2, neg0);
+      w[2 * wi] = *reinterpret_cast<uint32_t*>(&d01);
+      w[2 * wi + 1] = *reinterpret_cast<uint32_t*>(&d23);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+cudaError_t gemm_w8_two_pass(const void* weight, const bf16* scales, const bf16* bias,
+                             const bf16* input, bf16* output, int m, int n, int k,
+                             const Scratch& sc, cudaStream_t stream) {
+  const size_t row_bytes = size_t(k) * 2;
+  int block = int(sc.bytes / row_bytes) / 256 * 256;
+  if (block <= 0) return cudaErrorMemoryAllocation;
+  if (block > n) block = n;
+  const int groups = (k + 63) / 64;
+  const int8_t* q = static_cast<const int8_t*>(weight);
+  const uint16_t* sb = reinterpret_cast<const uint16_t*>(scales);
+  bf16* wb = static_cast<bf16*>(sc.ptr);
+  for (int n0 = 0; n0 < n; n0 += block) {
+    const int nr = n - n0 < block ? n - n0 : block;
+    const size_t chunks = size_t(nr) * (k / 16);
+    int grid = int((chunks + 255) / 256);
+    if (grid > 148 * 8) grid = 148 * 8;
+    dequant_w8_kernel<<<grid, 256, 0, stream>>>(q + size_t(n0) * k, sb + size_t(n0) * groups,
+                                                groups, wb, nr, k);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    e = launch_tile<false>(choose_tile(false, m, nr), wb, nullptr, bias ? bias + n0 : nullptr,
+                           input, output + n0, m, nr, k, n, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t reserve_gemm_scratch(size_t bytes) {
+  Scratch sc;
+  return scratch_get(bytes == 0 ? kScratchCap : bytes, true, &sc);
+}
+
 cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
                            const bf16* bias, const bf16* input, bf16* output,
                            int m, int n, int k, cudaStream_t stream) {
+  if (w8 && m >= kTwoPassMinTokens && !getenv("B200_GEMM_ONE_PASS")) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(stream, &cap);
+    Scratch sc;
+    if (scratch_get(size_t(n) * k * 2, cap == cudaStreamCaptureStatusNone, &sc) ==
+        cudaSuccess) {
+      return gemm_w8_two_pass(weight, scales, bias, input, output, m, n, k, sc, stream);
+    }
+  }
   const Tile t = choose_tile(w8, m, n);
-  return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, stream)
-            : launch_tile<false>(t, weight, scales, bias, input, output, m, n, k, stream);
+  return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, n, stream)
+            : launch_tile<false>(t, weight, scales, bias, input, output, m, n, k, n, stream);
 }
 
 }  // namespace b200

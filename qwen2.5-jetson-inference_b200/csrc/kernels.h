@@ -35,4 +35,8 @@ cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
                            const bf16* bias, const bf16* input, bf16* output,
                            int m, int n, int k, cudaStream_t stream);
 
+// Allocates (once per device) the BF16 weight buffer of the two-pass W8A16
+// prefill path; bytes == 0 means the default cap.
+cudaError_t reserve_gemm_scratch(size_t bytes);
+
 }  // namespace b200

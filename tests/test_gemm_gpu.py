@@ -151,3 +151,37 @@ def test_gemm_output_guard_band_and_status(b200, oracle, cuda):
     got = oracle.bf16_to_f32(to_bits(y))
     assert np.all(np.abs(got - exp) <= w8_tol(exp))
     assert b200.device_status() == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(1024, 896, 4864), (2048, 896, 151936), (1100, 4864, 904)])
+def test_w8a16_one_pass_and_two_pass_agree(b200, oracle, cuda, m, k, n):
+    """Large-M W8A16 runs as dequantise-once + BF16 tensor-core GEMM; the
+    one-pass in-kernel dequant path (B200_GEMM_ONE_PASS) must agree with it
+    (both multiply bf16(q*s); only the FP32 accumulation order may differ)."""
+    import os
+    import torch
+    assert b200.ABI.b200_gemm_reserve_scratch(0) == 0
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m + n)
+    w = torch.randn(n, k, generator=g, device=cuda) * 0.02
+    q, s = b200.quantize_groupwise(w)
+    bias = (torch.randn(n, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g, device=cuda).to(torch.bfloat16)
+    two = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    one = torch.empty_like(two)
+    b200.gemm_w8a16(q, s, 64, bias, x, two, m, n, k)
+    os.environ["B200_GEMM_ONE_PASS"] = "1"
+    try:
+        b200.gemm_w8a16(q, s, 64, bias, x, one, m, n, k)
+    finally:
+        del os.environ["B200_GEMM_ONE_PASS"]
+    torch.cuda.synchronize()
+    a, r = two.float(), one.float()
+    assert bool(((a - r).abs() <= r.abs() * 2.0 ** -7 * 1.01 + 1e-4).all())
+    rows = [0, m // 2, m - 1]
+    qn, sn = q.cpu().numpy(), s.view(torch.int16).cpu().numpy().view(np.uint16)
+    xb = x[rows].view(torch.int16).cpu().numpy().view(np.uint16)
+    bb = bias.view(torch.int16).cpu().numpy().view(np.uint16)
+    exp = oracle.bf16_to_f32(oracle.linear_w8a16(qn, sn, bb, xb, gemm=True))
+    got = a[rows].cpu().numpy()
+    assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
