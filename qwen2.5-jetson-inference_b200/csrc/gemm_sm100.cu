@@ -1240,8 +1240,11 @@ cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(stream, &cap);
     Scratch sc;
-    if (scratch_get(size_t(n) * k * 2, cap == cudaStreamCaptureStatusNone, &sc) ==
-        cudaSuccess) {
+    // The buffer is allocated at its full cap (not this call's size) so that
+    // a later, larger GEMM can still use it; a buffer too small for one
+    // 256-row block of this K falls back to the one-pass kernel.
+    if (scratch_get(kScratchCap, cap == cudaStreamCaptureStatusNone, &sc) == cudaSuccess &&
+        sc.bytes / (size_t(k) * 2) >= 256) {
       return gemm_w8_two_pass(weight, scales, bias, input, output, m, n, k, sc, stream);
     }
   }
