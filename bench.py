@@ -372,6 +372,24 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
     forced = e2e.run("reference", model, prompt, precision="w16a16", new_tokens=2,
                      warmup=0, repeat=1, force_tokens=cub)
     out["reference_custom_vs_cublas_teacher_forced_w16a16"] = e2e.forced_agreement(forced, cub)
+    # The native engine (include/b200_engine.h): same model, fused layers,
+    # one CUDA graph per decode step.
+    eng_mod = importlib.import_module("qwen25_b200.engine")
+    out["native_engine"] = []
+    for prec in ("w8a16", "w16a16"):
+        eng = eng_mod.Engine(model, prec, max_seq=256)
+        for _ in range(warmup):
+            eng.generate(prompt, new_tokens)
+        runs = [eng.generate(prompt, new_tokens) for _ in range(repeat)]
+        toks = runs[0][0]
+        ref = tokens[("reference", prec, "custom")]
+        out["native_engine"].append({
+            "precision": prec,
+            "decode_tok_s": round(statistics.median(
+                (new_tokens - 1) * 1e3 / r[2] for r in runs), 1),
+            "ttft_ms": round(statistics.median(r[1] for r in runs), 3),
+            "token_identical_prefix_vs_reference_kernels": prefix(toks, ref)})
+        eng.close()
     cpu = e2e.run("reference", model, prompt, backend="cpu", precision="fp32",
                   new_tokens=16, warmup=0, repeat=1)
     out["cpu_fp32"] = {"decode_tok_s": round(cpu["decode_tok_s"][0], 2),

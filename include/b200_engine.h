@@ -1,0 +1,82 @@
+/*
+ * b200_engine.h - native batch-1 greedy decode engine for the Qwen2.5
+ * architecture on the b200 Linear kernels (C ABI).
+ *
+ * The reference runs this model in Qwen2Model (reference src/qwen2.cpp,
+ * include/infer/qwen2.hpp:41-54); this engine is the GPU-resident
+ * counterpart: same weights (qbin archives), same arithmetic at the BF16
+ * tensor boundaries, but q/k/v and gate/up weights concatenated, RMSNorm /
+ * SiLU*up / residual adds fused into the decode GEMVs, and each decode step
+ * one CUDA graph with the token and position kept on the device.
+ *
+ * All pointers are device pointers the caller owns and keeps alive for the
+ * engine's lifetime.  The engine allocates its activations and KV cache once
+ * in b200_engine_create.  Returns B200_OK or a B200_ERR_* / cudaError_t.
+ */
+#ifndef B200_ENGINE_H_
+#define B200_ENGINE_H_
+
+#include "b200_linear.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b200_engine* b200_engine_t;
+
+typedef struct {
+  int hidden;        /* 896 */
+  int intermediate;  /* 4864 */
+  int layers;        /* 24 */
+  int heads;         /* 14 (head_dim = hidden / heads must be 64) */
+  int kv_heads;      /* 2 */
+  int vocab;         /* 151936 (multiple of 8) */
+  int max_seq;       /* KV cache length (<= 8192) */
+  float eps;         /* RMSNorm epsilon */
+  float theta;       /* RoPE base */
+  int w8;            /* 1: W8A16 Linear weights (group 64), 0: BF16 */
+} b200_engine_config;
+
+/* One layer.  qkv_* are the q, k, v projections concatenated by rows
+ * ([q; k; v], (heads + 2 kv_heads) * head_dim rows), gate_up_* the gate and
+ * up projections ([gate; up], 2 * intermediate rows).  *_s are the BF16
+ * group-64 scales (W8A16 only, else NULL).  Norm gains are BF16. */
+typedef struct {
+  const void* qkv_w;
+  const uint16_t* qkv_s;
+  const uint16_t* qkv_b;
+  const void* o_w;
+  const uint16_t* o_s;
+  const void* gate_up_w;
+  const uint16_t* gate_up_s;
+  const void* down_w;
+  const uint16_t* down_s;
+  const uint16_t* input_norm;
+  const uint16_t* post_norm;
+} b200_engine_layer;
+
+/* embed: [vocab, hidden] BF16 (also the tied LM head). */
+int b200_engine_create(b200_engine_t* engine, const b200_engine_config* config,
+                       const b200_engine_layer* layers, const uint16_t* embed,
+                       const uint16_t* final_norm, b200_stream_t stream);
+int b200_engine_destroy(b200_engine_t engine);
+
+/* Prefill the prompt (host token ids, n <= max_seq) from position 0; the
+ * first generated token becomes output token 0.  Asynchronous. */
+int b200_engine_prefill(b200_engine_t engine, const int* prompt, int n);
+
+/* `steps` greedy decode steps (one graph replay each), each appending one
+ * token to the output list.  Asynchronous. */
+int b200_engine_decode(b200_engine_t engine, int steps);
+
+/* Copies the first `count` output tokens to host memory (synchronises). */
+int b200_engine_tokens(b200_engine_t engine, int* out, int count);
+
+/* Copies the BF16 logits of the last step to host memory (synchronises). */
+int b200_engine_logits(b200_engine_t engine, uint16_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_ENGINE_H_ */

@@ -21,7 +21,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libb200linear.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu",
+SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu", "engine.cu",
            "sharded.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
@@ -36,7 +36,7 @@ def nvcc() -> str:
 
 
 def _headers():
-    out = [os.path.join(INCLUDE, "b200_linear.h")]
+    out = [os.path.join(INCLUDE, "b200_linear.h"), os.path.join(INCLUDE, "b200_engine.h")]
     out += [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     return out
 

@@ -20,6 +20,10 @@ __device__ __forceinline__ float bf16_hi(uint32_t pair) {
   return __uint_as_float(pair & 0xffff0000u);
 }
 
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
 // Exact int8 -> float for one byte of a packed word.
 // Published magic-number method (the one FasterTransformer / CUTLASS use for
 // fast integer-to-float conversion): XOR the byte with 0x80 to get u = q+128,

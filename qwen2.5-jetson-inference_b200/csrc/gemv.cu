@@ -452,7 +452,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
                  const bf16* __restrict__ input, bf16* __restrict__ output,
                  int n_rows, int k_arg, int stages, int stage_bytes,
                  int w_tile_bytes, float* __restrict__ block_value,
-                 int* __restrict__ block_index) {
+                 int* __restrict__ block_index, const GemvFusion fusion) {
   constexpr int kEPC = kW8 ? 16 : 8;  // elements per 16-byte chunk
   constexpr int kPlanes = kEPC / 4;
   static_assert(kWPR == 1 || (kLPR == 32 && kR == 1), "split rows use whole warps");
@@ -484,6 +484,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   float* red_v = reinterpret_cast<float*>(bars + 2 * stages + 1);
   int* red_i = reinterpret_cast<int*>(red_v + kConsumerWarps);
   float* red_part = reinterpret_cast<float*>(red_i + kConsumerWarps);  // [2][warps]
+  float* norm_red = red_part + 2 * kConsumerWarps;                       // [warps]
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
@@ -525,13 +526,49 @@ gemv_bulk_kernel(const void* __restrict__ weight,
     // ------------------------------------------------------------ consumers
     const int ct = threadIdx.x - 32;
     pdl_wait_primary();
+    float norm_scale = 1.0f;
+    if (fusion.in_mode == 1) {
+      // RMSNorm of the input: FP32 sum of squares over the consumer threads.
+      float ss = 0.0f;
+      for (int e4 = ct; e4 < (k >> 2); e4 += kConsumerWarps * 32) {
+        const uint2 raw = reinterpret_cast<const uint2*>(input)[e4];
+        const float a = bf16_lo(raw.x), b = bf16_hi(raw.x);
+        const float c = bf16_lo(raw.y), d = bf16_hi(raw.y);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(b, b, ss);
+        ss = fmaf(c, c, ss);
+        ss = fmaf(d, d, ss);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) norm_red[warp - 1] = ss;
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      float total = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) total += norm_red[w];
+      norm_scale = rsqrtf(total / float(k) + fusion.eps);
+    }
     // x -> FP32 planes: xs[p * chunks + c] = x[c*kEPC + 4p .. +3].
     for (int e4 = ct; e4 < (k >> 2); e4 += kConsumerWarps * 32) {
       const uint2 raw = reinterpret_cast<const uint2*>(input)[e4];
       const int c = (e4 * 4) / kEPC;
       const int p = ((e4 * 4) % kEPC) >> 2;
-      xs[p * chunks + c] = make_float4(bf16_lo(raw.x), bf16_hi(raw.x),
-                                       bf16_lo(raw.y), bf16_hi(raw.y));
+      float4 v = make_float4(bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y),
+                             bf16_hi(raw.y));
+      if (fusion.in_mode == 1) {
+        const uint2 wr = reinterpret_cast<const uint2*>(fusion.norm_w)[e4];
+        v.x = bf16_round(v.x * bf16_lo(wr.x) * norm_scale);
+        v.y = bf16_round(v.y * bf16_hi(wr.x) * norm_scale);
+        v.z = bf16_round(v.z * bf16_lo(wr.y) * norm_scale);
+        v.w = bf16_round(v.w * bf16_hi(wr.y) * norm_scale);
+      } else if (fusion.in_mode == 2) {
+        const uint2 ur = reinterpret_cast<const uint2*>(input + k)[e4];
+        v.x = bf16_round(v.x / (1.0f + expf(-v.x)) * bf16_lo(ur.x));
+        v.y = bf16_round(v.y / (1.0f + expf(-v.y)) * bf16_hi(ur.x));
+        v.z = bf16_round(v.z / (1.0f + expf(-v.z)) * bf16_lo(ur.y));
+        v.w = bf16_round(v.w / (1.0f + expf(-v.w)) * bf16_hi(ur.y));
+      }
+      xs[p * chunks + c] = v;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
@@ -625,7 +662,12 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         if (ok && ll == 0 && ksub == 0 && row < n_rows) {
           const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
           const bf16 y = __float2bfloat16_rn(v + b);
-          output[row] = y;
+          if (fusion.residual != nullptr) {
+            fusion.residual[row] = __float2bfloat16_rn(
+                __bfloat162float(fusion.residual[row]) + __bfloat162float(y));
+          } else {
+            output[row] = y;
+          }
           argmax_update(best, best_index, __bfloat162float(y), row);
         }
       }
@@ -716,7 +758,7 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
       best.stage_bytes = st;
       best.w_tile_bytes = wt;
       best.smem = stages * st + x_bytes + 8 * 2 * stages + 8 +
-                  8 * kConsumerWarps + 8 * kConsumerWarps;
+                  8 * kConsumerWarps + 8 * kConsumerWarps + 4 * kConsumerWarps;
       best.grid = tiles < sms ? tiles : sms;
     }
   }
@@ -726,7 +768,8 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
 template <bool kW8, int kLPR, int kR, int kWPR>
 cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                         const bf16* b, const bf16* x, bf16* y, int n, int k,
-                        float* bv, int* bi, cudaStream_t stream) {
+                        float* bv, int* bi, cudaStream_t stream,
+                        const GemvFusion& fusion) {
   auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896>
                          : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0>;
   cudaError_t e = cudaFuncSetAttribute(
@@ -743,26 +786,26 @@ cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, w, s, b, x, y, n, k, p.stages,
-                            p.stage_bytes, p.w_tile_bytes, bv, bi);
+                            p.stage_bytes, p.w_tile_bytes, bv, bi, fusion);
 }
 
 template <bool kW8>
 cudaError_t dispatch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                           const bf16* b, const bf16* x, bf16* y, int n, int k,
-                          float* bv, int* bi, cudaStream_t st) {
-  if (p.wpr == 4) return launch_bulk<kW8, 32, 1, 4>(p, w, s, b, x, y, n, k, bv, bi, st);
-  if (p.wpr == 2) return launch_bulk<kW8, 32, 1, 2>(p, w, s, b, x, y, n, k, bv, bi, st);
+                          float* bv, int* bi, cudaStream_t st, const GemvFusion& f) {
+  if (p.wpr == 4) return launch_bulk<kW8, 32, 1, 4>(p, w, s, b, x, y, n, k, bv, bi, st, f);
+  if (p.wpr == 2) return launch_bulk<kW8, 32, 1, 2>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   if (p.lpr == 8) {
-    return p.r == 2 ? launch_bulk<kW8, 8, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
-                    : launch_bulk<kW8, 8, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
+    return p.r == 2 ? launch_bulk<kW8, 8, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f)
+                    : launch_bulk<kW8, 8, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   }
   if (p.lpr == 16) {
-    return p.r == 2 ? launch_bulk<kW8, 16, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
-                    : launch_bulk<kW8, 16, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
+    return p.r == 2 ? launch_bulk<kW8, 16, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f)
+                    : launch_bulk<kW8, 16, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   }
-  if (p.r == 4) return launch_bulk<kW8, 32, 4, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
-  return p.r == 2 ? launch_bulk<kW8, 32, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st)
-                  : launch_bulk<kW8, 32, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st);
+  if (p.r == 4) return launch_bulk<kW8, 32, 4, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f);
+  return p.r == 2 ? launch_bulk<kW8, 32, 2, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f)
+                  : launch_bulk<kW8, 32, 1, 1>(p, w, s, b, x, y, n, k, bv, bi, st, f);
 }
 
 struct GemvConfig {
@@ -862,12 +905,18 @@ bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
 cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
                         const bf16* bias, const bf16* input, bf16* output,
                         int n, int k, float* block_value, int* block_index,
-                        cudaStream_t stream, int* grid_out) {
+                        cudaStream_t stream, int* grid_out,
+                        const GemvFusion* fusion) {
+  const GemvFusion nofusion;
+  const GemvFusion& f = fusion ? *fusion : nofusion;
+  const bool fused = fusion != nullptr &&
+                     (f.in_mode != 0 || f.residual != nullptr);
   if (n <= 0) {
     if (grid_out) *grid_out = 0;
     return cudaSuccess;
   }
   if (!gemv_uses_fast_path(w8, weight, input, k)) {
+    if (fused) return cudaErrorNotSupported;
     return w8 ? launch_generic<true>(weight, scales, bias, input, output, n, k,
                                      block_value, block_index, stream, grid_out)
               : launch_generic<false>(weight, scales, bias, input, output, n,
@@ -884,11 +933,13 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
     if (p.lpr > 0) {
       if (grid_out) *grid_out = p.grid;
       return w8 ? dispatch_bulk<true>(p, weight, scales, bias, input, output, n,
-                                      k, block_value, block_index, stream)
+                                      k, block_value, block_index, stream, f)
                 : dispatch_bulk<false>(p, weight, scales, bias, input, output,
-                                       n, k, block_value, block_index, stream);
+                                       n, k, block_value, block_index, stream, f);
     }
   }
+  // The fusions exist only in the TMA-bulk kernel.
+  if (fused) return cudaErrorNotSupported;
   const int chunks = w8 ? k / 16 : k / 8;
   const GemvConfig c = choose_config(n, chunks, block_value != nullptr);
   if (w8) {

@@ -8,6 +8,21 @@ namespace b200 {
 
 using bf16 = __nv_bfloat16;
 
+// Optional fusions of the decode GEMV, used by the native decode engine
+// (engine.cu) to fold the layers around a Linear into its load and store:
+//   in_mode 1: x' = bf16(x * w * rsqrt(mean(x^2) + eps)) (RMSNorm of the
+//              input, reference src/cuda/kernels.cu:64-116);
+//   in_mode 2: the input holds [gate | up] (2 x in_features) and
+//              x' = bf16(silu(gate) * up) (reference kernels.cu:302-324);
+//   residual:  residual[n] = bf16(residual[n] + bf16(y[n])) replaces the
+//              output store (reference add_inplace_bf16, kernels.cu:285-300).
+struct GemvFusion {
+  int in_mode = 0;
+  const bf16* norm_w = nullptr;
+  float eps = 0.0f;
+  bf16* residual = nullptr;
+};
+
 // gemv.cu
 bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
                          int k);
@@ -16,7 +31,8 @@ bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
 cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
                         const bf16* bias, const bf16* input, bf16* output,
                         int n, int k, float* block_value, int* block_index,
-                        cudaStream_t stream, int* grid_out);
+                        cudaStream_t stream, int* grid_out,
+                        const GemvFusion* fusion = nullptr);
 cudaError_t launch_argmax_partials(const float* block_value,
                                    const int* block_index, int count,
                                    int* argmax, cudaStream_t stream);

@@ -1,0 +1,145 @@
+"""Python face of the native decode engine (include/b200_engine.h).
+
+Loads a QWENBIN1 model directory (config.json + model.w16a16.qbin or
+model.w8a16.qbin), concatenates q/k/v and gate/up rows on the device, and
+runs prefill + graph-replayed greedy decode.  Same model and weights as the
+reference engine (reference src/qwen2.cpp); see csrc/engine.cu.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import time
+
+import numpy as np
+import torch
+
+from . import ABI, _check
+from . import qbin
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+
+
+class EngineConfig(ctypes.Structure):
+    _fields_ = [("hidden", _i), ("intermediate", _i), ("layers", _i), ("heads", _i),
+                ("kv_heads", _i), ("vocab", _i), ("max_seq", _i), ("eps", ctypes.c_float),
+                ("theta", ctypes.c_float), ("w8", _i)]
+
+
+class EngineLayer(ctypes.Structure):
+    _fields_ = [(n, _p) for n in ("qkv_w", "qkv_s", "qkv_b", "o_w", "o_s", "gate_up_w",
+                                  "gate_up_s", "down_w", "down_s", "input_norm", "post_norm")]
+
+
+for _name, (_args, _res) in {
+    "b200_engine_create": ([ctypes.POINTER(_p), ctypes.POINTER(EngineConfig),
+                            ctypes.POINTER(EngineLayer), _p, _p, _p], _i),
+    "b200_engine_destroy": ([_p], _i),
+    "b200_engine_prefill": ([_p, ctypes.POINTER(_i), _i], _i),
+    "b200_engine_decode": ([_p, _i], _i),
+    "b200_engine_tokens": ([_p, ctypes.POINTER(_i), _i], _i),
+    "b200_engine_logits": ([_p, ctypes.POINTER(ctypes.c_uint16)], _i),
+}.items():
+    _fn = getattr(ABI, _name)
+    _fn.argtypes = _args
+    _fn.restype = _res
+
+
+def _dev(a: np.ndarray, device):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16).copy()).to(device).view(torch.bfloat16)
+    return torch.from_numpy(a.copy()).to(device)
+
+
+class Engine:
+    """Greedy batch-1 decoder on one GPU."""
+
+    def __init__(self, model_dir: str, precision: str = "w8a16", max_seq: int = 256,
+                 device="cuda"):
+        cfg = json.load(open(os.path.join(model_dir, "config.json")))
+        arch = qbin.load_archive(os.path.join(model_dir, qbin.ARCHIVE_NAMES[precision]))
+        self.device = torch.device(device)
+        self.w8 = precision == "w8a16"
+        self.cfg = cfg
+        keep = []  # device tensors referenced by the engine
+
+        def t(name):
+            x = _dev(arch[name], self.device)
+            keep.append(x)
+            return x
+
+        def cat(names):
+            x = torch.cat([_dev(arch[n], self.device) for n in names], 0).contiguous()
+            keep.append(x)
+            return x
+
+        layers = (EngineLayer * cfg["num_hidden_layers"])()
+        for i in range(cfg["num_hidden_layers"]):
+            p = f"model.layers.{i}."
+            a = p + "self_attn."
+            m = p + "mlp."
+            L = layers[i]
+            L.qkv_w = cat([a + "q_proj.weight", a + "k_proj.weight", a + "v_proj.weight"]).data_ptr()
+            L.qkv_b = cat([a + "q_proj.bias", a + "k_proj.bias", a + "v_proj.bias"]).data_ptr()
+            L.o_w = t(a + "o_proj.weight").data_ptr()
+            L.gate_up_w = cat([m + "gate_proj.weight", m + "up_proj.weight"]).data_ptr()
+            L.down_w = t(m + "down_proj.weight").data_ptr()
+            if self.w8:
+                L.qkv_s = cat([a + f"{x}_proj.weight.scale" for x in "qkv"]).data_ptr()
+                L.o_s = t(a + "o_proj.weight.scale").data_ptr()
+                L.gate_up_s = cat([m + "gate_proj.weight.scale",
+                                   m + "up_proj.weight.scale"]).data_ptr()
+                L.down_s = t(m + "down_proj.weight.scale").data_ptr()
+            L.input_norm = t(p + "input_layernorm.weight").data_ptr()
+            L.post_norm = t(p + "post_attention_layernorm.weight").data_ptr()
+        head = "lm_head.weight" if "lm_head.weight" in arch else "model.embed_tokens.weight"
+        embed = t("model.embed_tokens.weight")
+        if head != "model.embed_tokens.weight":
+            raise ValueError("untied LM head is not supported by this engine")
+        fnorm = t("model.norm.weight")
+        self._keep = keep
+        self.config = EngineConfig(cfg["hidden_size"], cfg["intermediate_size"],
+                                   cfg["num_hidden_layers"], cfg["num_attention_heads"],
+                                   cfg["num_key_value_heads"], cfg["vocab_size"], max_seq,
+                                   cfg.get("rms_norm_eps", 1e-6), cfg.get("rope_theta", 1e6),
+                                   1 if self.w8 else 0)
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.handle = _p()
+        _check(ABI.b200_engine_create(ctypes.byref(self.handle), ctypes.byref(self.config),
+                                      layers, embed.data_ptr(), fnorm.data_ptr(),
+                                      self.stream.cuda_stream), "engine_create")
+        torch.cuda.synchronize()
+
+    def generate(self, prompt, new_tokens: int):
+        """(tokens, ttft_ms, decode_ms): prefill, then new_tokens-1 graph steps."""
+        arr = (_i * len(prompt))(*prompt)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        _check(ABI.b200_engine_prefill(self.handle, arr, len(prompt)), "engine_prefill")
+        first = (_i * 1)()
+        _check(ABI.b200_engine_tokens(self.handle, first, 1), "engine_tokens")
+        t1 = time.perf_counter()
+        _check(ABI.b200_engine_decode(self.handle, new_tokens - 1), "engine_decode")
+        out = (_i * new_tokens)()
+        _check(ABI.b200_engine_tokens(self.handle, out, new_tokens), "engine_tokens")
+        t2 = time.perf_counter()
+        return list(out), (t1 - t0) * 1e3, (t2 - t1) * 1e3
+
+    def logits(self) -> np.ndarray:
+        buf = (ctypes.c_uint16 * self.config.vocab)()
+        _check(ABI.b200_engine_logits(self.handle, buf), "engine_logits")
+        return np.frombuffer(buf, dtype=np.uint16).copy()
+
+    def close(self):
+        if self.handle:
+            ABI.b200_engine_destroy(self.handle)
+            self.handle = _p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -171,3 +171,16 @@ def write_model(directory: str, config: dict, seed: int = 0,
     tensors = synthetic_qwen2(config, seed)
     for p in precisions:
         write_archive(os.path.join(directory, ARCHIVE_NAMES[p]), tensors, p)
+
+
+def load_archive(path: str) -> dict:
+    """{name: numpy array} of an archive (BF16 as uint16 bit patterns), as
+    views of a read-only memory map."""
+    meta = read_records(path)
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    dt = {"float32": np.float32, "bfloat16": np.uint16, "int8": np.int8}
+    out = {}
+    for rec in meta["tensors"]:
+        raw = mm[DATA_OFFSET + rec["offset"]:DATA_OFFSET + rec["offset"] + rec["nbytes"]]
+        out[rec["name"]] = raw.view(dt[rec["dtype"]]).reshape(rec["shape"])
+    return out
