@@ -504,8 +504,23 @@ def run_reference(args):
 
 
 def run_case(args):
-    """One kernel, `warmup` + `steps` launches, for ncu captures (no timing)."""
+    """One kernel, `warmup` + `steps` launches, for ncu captures (no timing).
+    `engine_w8` / `engine_bf16`: the native engine on a 4-layer synthetic
+    Qwen2.5 (real widths), one prefill + `steps` graph-replayed decode steps."""
     torch.cuda.set_device(0)
+    if args.case.startswith("engine"):
+        import importlib
+        load_pkg()
+        e2e = importlib.import_module("qwen25_b200.e2e")
+        q = importlib.import_module("qwen25_b200.qbin")
+        eng = importlib.import_module("qwen25_b200.engine")
+        d = e2e.ensure_model("/tmp/b200_e2e_qwen2_4layer",
+                             dict(q.QWEN25_05B, num_hidden_layers=4), seed=0)
+        e = eng.Engine(d, "w8a16" if args.case == "engine_w8" else "w16a16", max_seq=256)
+        toks, ttft, dec = e.generate(e2e.prompt_ids(32, seed=1), args.steps + 1)
+        print(json.dumps({"case": args.case, "ttft_ms": ttft, "decode_ms": dec}))
+        e.close()
+        return
     dev = torch.device("cuda", 0)
     b200 = load_pkg()
     gen = torch.Generator(device=dev)
