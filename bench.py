@@ -372,24 +372,26 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
     forced = e2e.run("reference", model, prompt, precision="w16a16", new_tokens=2,
                      warmup=0, repeat=1, force_tokens=cub)
     out["reference_custom_vs_cublas_teacher_forced_w16a16"] = e2e.forced_agreement(forced, cub)
-    # The native engine (include/b200_engine.h): same model, fused layers,
-    # one CUDA graph per decode step.
+    # The native engine (include/b200_engine.h): same model, fused layers;
+    # decode as one persistent kernel, or one CUDA graph per step.
     eng_mod = importlib.import_module("qwen25_b200.engine")
     out["native_engine"] = []
     for prec in ("w8a16", "w16a16"):
-        eng = eng_mod.Engine(model, prec, max_seq=256)
-        for _ in range(warmup):
-            eng.generate(prompt, new_tokens)
-        runs = [eng.generate(prompt, new_tokens) for _ in range(repeat)]
-        toks = runs[0][0]
-        ref = tokens[("reference", prec, "custom")]
-        out["native_engine"].append({
-            "precision": prec,
-            "decode_tok_s": round(statistics.median(
-                (new_tokens - 1) * 1e3 / r[2] for r in runs), 1),
-            "ttft_ms": round(statistics.median(r[1] for r in runs), 3),
-            "token_identical_prefix_vs_reference_kernels": prefix(toks, ref)})
-        eng.close()
+        for mode in ("persistent", "graph"):
+            eng = eng_mod.Engine(model, prec, max_seq=256, mode=mode)
+            for _ in range(warmup):
+                eng.generate(prompt, new_tokens)
+            runs = [eng.generate(prompt, new_tokens) for _ in range(repeat)]
+            toks = runs[0][0]
+            ref = tokens[("reference", prec, "custom")]
+            out["native_engine"].append({
+                "precision": prec, "decode_mode": mode,
+                "decode_tok_s": round(statistics.median(
+                    (new_tokens - 1) * 1e3 / r[2] for r in runs), 1),
+                "ttft_ms": round(statistics.median(r[1] for r in runs), 3),
+                "token_identical_prefix_vs_reference_kernels": prefix(toks, ref),
+                "device_status": eng.device_status()})
+            eng.close()
     cpu = e2e.run("reference", model, prompt, backend="cpu", precision="fp32",
                   new_tokens=16, warmup=0, repeat=1)
     out["cpu_fp32"] = {"decode_tok_s": round(cpu["decode_tok_s"][0], 2),
@@ -505,8 +507,9 @@ def run_reference(args):
 
 def run_case(args):
     """One kernel, `warmup` + `steps` launches, for ncu captures (no timing).
-    `engine_w8` / `engine_bf16`: the native engine on a 4-layer synthetic
-    Qwen2.5 (real widths), one prefill + `steps` graph-replayed decode steps."""
+    `engine_w8` / `engine_bf16` (+ `_graph`): the native engine on a 4-layer
+    synthetic Qwen2.5 (real widths), one prefill + `steps` decode steps in
+    the persistent kernel (or as graph replays)."""
     torch.cuda.set_device(0)
     if args.case.startswith("engine"):
         import importlib
@@ -516,7 +519,9 @@ def run_case(args):
         eng = importlib.import_module("qwen25_b200.engine")
         d = e2e.ensure_model("/tmp/b200_e2e_qwen2_4layer",
                              dict(q.QWEN25_05B, num_hidden_layers=4), seed=0)
-        e = eng.Engine(d, "w8a16" if args.case == "engine_w8" else "w16a16", max_seq=256)
+        e = eng.Engine(d, "w8a16" if args.case.startswith("engine_w8") else "w16a16",
+                       max_seq=256,
+                       mode="graph" if args.case.endswith("_graph") else "persistent")
         toks, ttft, dec = e.generate(e2e.prompt_ids(32, seed=1), args.steps + 1)
         print(json.dumps({"case": args.case, "ttft_ms": ttft, "decode_ms": dec}))
         e.close()

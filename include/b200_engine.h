@@ -65,9 +65,35 @@ int b200_engine_destroy(b200_engine_t engine);
  * first generated token becomes output token 0.  Asynchronous. */
 int b200_engine_prefill(b200_engine_t engine, const int* prompt, int n);
 
-/* `steps` greedy decode steps (one graph replay each), each appending one
- * token to the output list.  Asynchronous. */
+/* `steps` greedy decode steps, each appending one token to the output list
+ * (prompt length + all decoded steps <= max_seq, else B200_ERR_TOO_LARGE).
+ * Asynchronous. */
 int b200_engine_decode(b200_engine_t engine, int steps);
+
+/* Decode modes.  PERSISTENT (the default where the shapes allow it): all
+ * steps of one b200_engine_decode call in one cooperative kernel, one CTA
+ * per SM, layers chained by grid-wide barriers while each CTA streams its
+ * weight tiles ahead into shared memory.  GRAPH: one CUDA graph replay per
+ * step (146 kernel launches for the 24-layer model). */
+#define B200_ENGINE_DECODE_PERSISTENT 0
+#define B200_ENGINE_DECODE_GRAPH 1
+/* Selects the decode mode (B200_ERR_TOO_LARGE: the persistent kernel does
+ * not take this model's shapes / shared-memory needs). */
+int b200_engine_set_decode_mode(b200_engine_t engine, int mode);
+/* Profiling timeline of the persistent kernel: with barriers > 0 the next
+ * decode calls record, for their first `barriers` grid barriers, each CTA's
+ * arrival and release times (global timer, ns); 0 turns it off.  Allocates
+ * a device buffer of grid x barriers x 16 bytes. */
+int b200_engine_set_trace(b200_engine_t engine, int barriers);
+/* Copies the timeline ([cta][barrier][arrive, leave]) to host memory when
+ * out != NULL (synchronises); returns the CTA count (0: tracing off). */
+int b200_engine_read_trace(b200_engine_t engine, unsigned long long* out);
+/* The current decode mode. */
+int b200_engine_decode_mode(b200_engine_t engine);
+/* Device-side error word of the persistent kernel (B200_DEVICE_*; a bounded
+ * wait that expired).  Synchronises the engine's stream; clear != 0 resets
+ * it. */
+int b200_engine_device_status(b200_engine_t engine, int clear);
 
 /* Copies the first `count` output tokens to host memory (synchronises). */
 int b200_engine_tokens(b200_engine_t engine, int* out, int count);

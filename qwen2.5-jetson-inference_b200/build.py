@@ -22,6 +22,7 @@ LIB = os.path.join(HERE, "libb200linear.so")
 INCLUDE = os.path.join(REPO, "include")
 
 SOURCES = ["gemv.cu", "gemm_simt.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu", "engine.cu",
+           "decode_persistent.cu",
            "sharded.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",

@@ -31,8 +31,10 @@
 #include <vector>
 
 #include "b200_engine.h"
+#include "attention.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "persistent.h"
 
 struct b200_engine {
   b200_engine_config cfg;
@@ -48,6 +50,15 @@ struct b200_engine {
   int* lm_index;
   int *d_token, *d_pos, *d_step, *d_out, *d_prompt;
   cudaGraphExec_t graph = nullptr;
+  // persistent decode kernel (decode_persistent.cu)
+  b200::PersistPlan plan;
+  b200::PersistLayer* d_layers = nullptr;
+  unsigned* grid_words = nullptr;  // [0] barrier counter, [1] abort flag
+  int* d_status = nullptr;
+  int mode = B200_ENGINE_DECODE_GRAPH;
+  int h_pos = -1;  // position of the next decode step (-1: no prefill yet)
+  unsigned long long* trace = nullptr;  // persistent-kernel timeline (optional)
+  int trace_count = 0;
 };
 
 namespace b200 {
@@ -169,77 +180,25 @@ __global__ void rope_store_kernel(bf16* __restrict__ qkv, int qkv_dim, int heads
 }
 
 // Causal GQA attention for query rows t at positions pos0 + t (or *d_pos),
-// one CTA per (head, t): scores in shared memory, softmax with a block max
-// and sum, output = sum_p softmax_p * v_p.
+// one CTA per (head, t) over the cache rows written by rope_store_kernel
+// (attend_row, attention.cuh).
 __global__ void __launch_bounds__(128)
-attention_kernel(const bf16* __restrict__ qkv, int qkv_dim, const bf16* __restrict__ kcache,
-                 const bf16* __restrict__ vcache, bf16* __restrict__ out, int heads,
+attention_kernel(const bf16* __restrict__ qkv, int qkv_dim, const bf16* kcache,
+                 const bf16* vcache, bf16* __restrict__ out, int heads,
                  int kv_heads, int hd, int max_seq, int pos0, const int* __restrict__ d_pos) {
-  extern __shared__ float scores[];
-  __shared__ float qs[256];
-  __shared__ float red[4];
-  __shared__ float partial[2][256];
+  extern __shared__ float att_smem[];
+  __shared__ float qs[kHeadDim];
   pdl_launch_dependents();
   pdl_wait_primary();
   const int head = blockIdx.x, t = blockIdx.y;
   const int seq = (d_pos ? *d_pos : pos0) + t + 1;
   const int kvh = head / (heads / kv_heads);
   const bf16* q = qkv + size_t(t) * qkv_dim + head * hd;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = __bfloat162float(q[d]);
+  if (threadIdx.x < kHeadDim) qs[threadIdx.x] = __bfloat162float(q[threadIdx.x]);
   __syncthreads();
-  const float scale = rsqrtf(float(hd));
-  const bf16* kbase = kcache + size_t(kvh) * max_seq * hd;
-  const bf16* vbase = vcache + size_t(kvh) * max_seq * hd;
-  float mx = -FLT_MAX;
-  for (int p = threadIdx.x; p < seq; p += blockDim.x) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kbase + size_t(p) * hd);
-    float dot = 0.0f;
-    for (int c = 0; c < hd / 8; ++c) {
-      const uint4 w = kr[c];
-      dot = fmaf(qs[8 * c + 0], bf16_lo(w.x), dot);
-      dot = fmaf(qs[8 * c + 1], bf16_hi(w.x), dot);
-      dot = fmaf(qs[8 * c + 2], bf16_lo(w.y), dot);
-      dot = fmaf(qs[8 * c + 3], bf16_hi(w.y), dot);
-      dot = fmaf(qs[8 * c + 4], bf16_lo(w.z), dot);
-      dot = fmaf(qs[8 * c + 5], bf16_hi(w.z), dot);
-      dot = fmaf(qs[8 * c + 6], bf16_lo(w.w), dot);
-      dot = fmaf(qs[8 * c + 7], bf16_hi(w.w), dot);
-    }
-    scores[p] = dot * scale;
-    mx = fmaxf(mx, dot * scale);
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  float sum = 0.0f;
-  for (int p = threadIdx.x; p < seq; p += blockDim.x) {
-    const float e = expf(scores[p] - mx);
-    scores[p] = e;
-    sum += e;
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  const float denom = red[0] + red[1] + red[2] + red[3];
-  // Two threads per output dimension split the positions.
-  const int d = threadIdx.x % hd;
-  const int half = threadIdx.x / hd;  // 0 or 1 for hd = 64
-  float acc = 0.0f;
-  if (half < 2) {
-    for (int p = half; p < seq; p += 2) {
-      acc = fmaf(scores[p] / denom, __bfloat162float(vbase[size_t(p) * hd + d]), acc);
-    }
-    partial[half][d] = acc;
-  }
-  __syncthreads();
-  if (threadIdx.x < hd) {
-    out[size_t(t) * heads * hd + head * hd + threadIdx.x] =
-        __float2bfloat16_rn(partial[0][threadIdx.x] + partial[1][threadIdx.x]);
-  }
+  attend_row<128>(qs, kcache + size_t(kvh) * max_seq * hd, vcache + size_t(kvh) * max_seq * hd,
+                  seq, -1, nullptr, nullptr, att_smem, threadIdx.x, [] { __syncthreads(); },
+                  out + size_t(t) * heads * hd + head * hd);
 }
 
 // Final argmax of the LM head (lowest index on ties) feeding the next step:
@@ -347,7 +306,8 @@ int layer_forward(b200_engine* e, int l, int t_rows, bool decode) {
   ENGINE_TRY(launch(b200::rope_store_kernel, dim3(t_rows), dim3(256), 0, s, e->qkv, e->qkv_dim,
                     c.heads, c.kv_heads, hd, c.theta, 0, dpos, kc, vc, c.max_seq));
   ENGINE_TRY(launch(b200::attention_kernel, dim3(c.heads, t_rows), dim3(128),
-                    size_t(c.max_seq) * sizeof(float), s, (const bf16*)e->qkv, e->qkv_dim,
+                    b200::attend_smem_floats<128>(c.max_seq) * sizeof(float), s,
+                    (const bf16*)e->qkv, e->qkv_dim,
                     (const bf16*)kc, (const bf16*)vc, e->att, c.heads, c.kv_heads, hd,
                     c.max_seq, 0, dpos));
   if (decode) {
@@ -454,7 +414,8 @@ int b200_engine_create(b200_engine_t* out, const b200_engine_config* cfg,
   // Buffer sizes in bytes, each rounded to 256.
   const size_t sizes[] = {T * H * 2, T * H * 2, T * e->qkv_dim * 2, T * H * 2, T * H * 2,
                           T * 2 * I * 2, T * I * 2, V * 2, kv * 2, kv * 2, blocks * 4,
-                          blocks * 4, 64, 64, 64, T * 4 + 64, T * 4 + 64};
+                          blocks * 4, 64, 64, 64, T * 4 + 64, T * 4 + 64,
+                          size_t(c.layers) * sizeof(b200::PersistLayer), 64, 64};
   size_t total = 0;
   for (size_t sz : sizes) total += (sz + 255) / 256 * 256;
   cudaError_t err = cudaMalloc(&e->arena, total);
@@ -486,6 +447,27 @@ int b200_engine_create(b200_engine_t* out, const b200_engine_config* cfg,
   e->d_step = static_cast<int*>(take());
   e->d_out = static_cast<int*>(take());
   e->d_prompt = static_cast<int*>(take());
+  e->d_layers = static_cast<b200::PersistLayer*>(take());
+  e->grid_words = static_cast<unsigned*>(take());
+  e->d_status = static_cast<int*>(take());
+  std::vector<b200::PersistLayer> pl(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const b200_engine_layer& L = layers[l];
+    auto B = [](const uint16_t* q) { return reinterpret_cast<const bf16*>(q); };
+    pl[l] = {L.qkv_w, B(L.qkv_s), B(L.qkv_b), L.o_w, B(L.o_s), L.gate_up_w, B(L.gate_up_s),
+             L.down_w, B(L.down_s), B(L.input_norm), B(L.post_norm)};
+  }
+  err = cudaMemcpy(e->d_layers, pl.data(), pl.size() * sizeof(b200::PersistLayer),
+                   cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemset(e->d_status, 0, sizeof(int));
+  if (err != cudaSuccess) {
+    cudaFree(e->arena);
+    delete e;
+    return int(err);
+  }
+  e->plan = b200::plan_persistent(c.w8 != 0, c.hidden, c.intermediate, c.heads, c.kv_heads,
+                                  c.vocab, c.max_seq);
+  e->mode = e->plan.ok ? B200_ENGINE_DECODE_PERSISTENT : B200_ENGINE_DECODE_GRAPH;
   *out = e;
   return B200_OK;
 }
@@ -493,6 +475,7 @@ int b200_engine_create(b200_engine_t* out, const b200_engine_config* cfg,
 int b200_engine_destroy(b200_engine_t e) {
   if (e == nullptr) return B200_OK;
   if (e->graph) cudaGraphExecDestroy(e->graph);
+  if (e->trace) cudaFree(e->trace);
   cudaFree(e->arena);
   delete e;
   return B200_OK;
@@ -508,12 +491,112 @@ int b200_engine_prefill(b200_engine_t e, const int* prompt, int n) {
                     reinterpret_cast<const bf16*>(e->embed), (const int*)e->d_prompt,
                     e->cfg.hidden, e->x));
   for (int l = 0; l < e->cfg.layers; ++l) ENGINE_TRY(layer_forward(e, l, n, false));
-  return head_forward(e, n - 1, n, e->cfg.max_seq);
+  ENGINE_TRY(head_forward(e, n - 1, n, e->cfg.max_seq));
+  e->h_pos = n;
+  return B200_OK;
+}
+
+int b200_engine_set_decode_mode(b200_engine_t e, int mode) {
+  if (e == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  if (mode == B200_ENGINE_DECODE_GRAPH) {
+    e->mode = mode;
+    return B200_OK;
+  }
+  if (mode != B200_ENGINE_DECODE_PERSISTENT) return B200_ERR_INVALID_ARGUMENT;
+  if (!e->plan.ok) return B200_ERR_TOO_LARGE;
+  e->mode = mode;
+  return B200_OK;
+}
+
+int b200_engine_set_trace(b200_engine_t e, int barriers) {
+  if (e == nullptr || barriers < 0) return B200_ERR_INVALID_ARGUMENT;
+  if (e->trace) {
+    ENGINE_TRY(check(cudaStreamSynchronize(e->stream)));
+    cudaFree(e->trace);
+    e->trace = nullptr;
+    e->trace_count = 0;
+  }
+  if (barriers == 0) return B200_OK;
+  if (!e->plan.ok) return B200_ERR_TOO_LARGE;
+  const size_t bytes = size_t(e->plan.grid) * barriers * 2 * sizeof(unsigned long long);
+  ENGINE_TRY(check(cudaMalloc(&e->trace, bytes)));
+  ENGINE_TRY(check(cudaMemset(e->trace, 0, bytes)));
+  e->trace_count = barriers;
+  return B200_OK;
+}
+
+int b200_engine_read_trace(b200_engine_t e, unsigned long long* out) {
+  if (e == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  if (e->trace == nullptr) return 0;
+  if (out != nullptr) {
+    const size_t n = size_t(e->plan.grid) * e->trace_count * 2;
+    ENGINE_TRY(check(cudaMemcpyAsync(out, e->trace, n * sizeof(unsigned long long),
+                                     cudaMemcpyDeviceToHost, e->stream)));
+    ENGINE_TRY(check(cudaStreamSynchronize(e->stream)));
+  }
+  return e->plan.grid;
+}
+
+int b200_engine_decode_mode(b200_engine_t e) {
+  return e == nullptr ? B200_ERR_INVALID_ARGUMENT : e->mode;
+}
+
+int b200_engine_device_status(b200_engine_t e, int clear) {
+  if (e == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  int v = 0;
+  cudaError_t err = cudaMemcpyAsync(&v, e->d_status, sizeof(int), cudaMemcpyDeviceToHost,
+                                    e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (err == cudaSuccess && clear) err = cudaMemset(e->d_status, 0, sizeof(int));
+  if (err != cudaSuccess) return -int(err);
+  return v;
 }
 
 int b200_engine_decode(b200_engine_t e, int steps) {
   if (e == nullptr || steps < 0) return B200_ERR_INVALID_ARGUMENT;
   if (steps == 0) return B200_OK;
+  // Each step writes the KV cache at its position: the prompt plus the
+  // decoded tokens must fit max_seq.
+  if (e->h_pos < 0) return B200_ERR_INVALID_ARGUMENT;
+  if (steps > e->cfg.max_seq - e->h_pos) return B200_ERR_TOO_LARGE;
+  e->h_pos += steps;
+  if (e->mode == B200_ENGINE_DECODE_PERSISTENT) {
+    const auto& c = e->cfg;
+    b200::PersistArgs a = {};
+    a.layers = e->d_layers;
+    a.n_layers = c.layers;
+    a.hidden = c.hidden;
+    a.inter = c.intermediate;
+    a.heads = c.heads;
+    a.kv_heads = c.kv_heads;
+    a.vocab = c.vocab;
+    a.max_seq = c.max_seq;
+    a.eps = c.eps;
+    a.theta = c.theta;
+    a.embed = reinterpret_cast<const bf16*>(e->embed);
+    a.final_norm = reinterpret_cast<const bf16*>(e->final_norm);
+    a.x = e->x;
+    a.qkv = e->qkv;
+    a.att = e->att;
+    a.gu = e->gu;
+    a.logits = e->logits;
+    a.kcache = e->kcache;
+    a.vcache = e->vcache;
+    a.part_v = e->lm_value;
+    a.part_i = e->lm_index;
+    a.d_token = e->d_token;
+    a.d_pos = e->d_pos;
+    a.d_step = e->d_step;
+    a.d_out = e->d_out;
+    a.max_out = c.max_seq;
+    a.grid_counter = e->grid_words;
+    a.grid_abort = reinterpret_cast<int*>(e->grid_words + 1);
+    a.status = e->d_status;
+    a.trace = e->trace;
+    a.trace_count = e->trace_count;
+    a.steps = steps;
+    return check(b200::launch_persistent(c.w8 != 0, e->plan, a, e->stream));
+  }
   if (e->graph == nullptr) {
     cudaGraph_t g = nullptr;
     ENGINE_TRY(check(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal)));

@@ -2,7 +2,8 @@
 
 Loads a QWENBIN1 model directory (config.json + model.w16a16.qbin or
 model.w8a16.qbin), concatenates q/k/v and gate/up rows on the device, and
-runs prefill + graph-replayed greedy decode.  Same model and weights as the
+runs prefill + greedy decode (one persistent cooperative kernel for all
+decode steps by default, or one CUDA graph replay per step).  Same model and weights as the
 reference engine (reference src/qwen2.cpp); see csrc/engine.cu.
 """
 from __future__ import annotations
@@ -41,6 +42,11 @@ for _name, (_args, _res) in {
     "b200_engine_decode": ([_p, _i], _i),
     "b200_engine_tokens": ([_p, ctypes.POINTER(_i), _i], _i),
     "b200_engine_logits": ([_p, ctypes.POINTER(ctypes.c_uint16)], _i),
+    "b200_engine_set_decode_mode": ([_p, _i], _i),
+    "b200_engine_decode_mode": ([_p], _i),
+    "b200_engine_device_status": ([_p, _i], _i),
+    "b200_engine_set_trace": ([_p, _i], _i),
+    "b200_engine_read_trace": ([_p, _p], _i),
 }.items():
     _fn = getattr(ABI, _name)
     _fn.argtypes = _args
@@ -54,11 +60,14 @@ def _dev(a: np.ndarray, device):
     return torch.from_numpy(a.copy()).to(device)
 
 
+DECODE_MODES = {"persistent": 0, "graph": 1}
+
+
 class Engine:
     """Greedy batch-1 decoder on one GPU."""
 
     def __init__(self, model_dir: str, precision: str = "w8a16", max_seq: int = 256,
-                 device="cuda"):
+                 device="cuda", mode: str | None = None):
         cfg = json.load(open(os.path.join(model_dir, "config.json")))
         arch = qbin.load_archive(os.path.join(model_dir, qbin.ARCHIVE_NAMES[precision]))
         self.device = torch.device(device)
@@ -112,9 +121,40 @@ class Engine:
                                       layers, embed.data_ptr(), fnorm.data_ptr(),
                                       self.stream.cuda_stream), "engine_create")
         torch.cuda.synchronize()
+        if mode is not None:
+            self.set_mode(mode)
+
+    @property
+    def mode(self) -> str:
+        m = ABI.b200_engine_decode_mode(self.handle)
+        return {v: k for k, v in DECODE_MODES.items()}[m]
+
+    def set_mode(self, mode: str) -> None:
+        _check(ABI.b200_engine_set_decode_mode(self.handle, DECODE_MODES[mode]),
+               "engine_set_decode_mode")
+
+    def trace(self, barriers: int) -> None:
+        """Records the persistent kernel's per-CTA barrier timeline for the
+        first `barriers` grid barriers of the next decode calls."""
+        _check(ABI.b200_engine_set_trace(self.handle, barriers), "engine_set_trace")
+        self._trace_barriers = barriers
+
+    def read_trace(self) -> np.ndarray:
+        """[cta, barrier, (arrive, leave)] global-timer ns of the last decode."""
+        ctas = ABI.b200_engine_read_trace(self.handle, None)
+        if ctas <= 0:
+            return np.zeros((0, 0, 2), np.uint64)
+        buf = np.zeros((ctas, self._trace_barriers, 2), np.uint64)
+        rc = ABI.b200_engine_read_trace(self.handle, buf.ctypes.data)
+        if rc < 0:
+            _check(rc, "engine_read_trace")
+        return buf
+
+    def device_status(self, clear: bool = False) -> int:
+        return ABI.b200_engine_device_status(self.handle, 1 if clear else 0)
 
     def generate(self, prompt, new_tokens: int):
-        """(tokens, ttft_ms, decode_ms): prefill, then new_tokens-1 graph steps."""
+        """(tokens, ttft_ms, decode_ms): prefill, then new_tokens-1 decode steps."""
         arr = (_i * len(prompt))(*prompt)
         torch.cuda.synchronize()
         t0 = time.perf_counter()

@@ -1,7 +1,8 @@
 """The native decode engine (include/b200_engine.h) against the reference
 engine with the reference's own kernels, on the seeded synthetic 4-layer
-Qwen2.5 of tests/test_e2e_gpu.py: prefill logits (cosine), greedy tokens,
-and graph-replayed decode equal to step-by-step decode."""
+Qwen2.5 of tests/test_e2e_gpu.py: prefill logits (cosine), greedy tokens in
+both decode modes (persistent kernel, graph replay), determinism and
+restartability, and the max_seq bound."""
 import importlib
 
 import numpy as np
@@ -21,8 +22,9 @@ def mods(b200, cuda):
     return e2e, eng
 
 
+@pytest.mark.parametrize("mode", ["persistent", "graph"])
 @pytest.mark.parametrize("precision", ["w16a16", "w8a16"])
-def test_engine_matches_reference_engine(mods, oracle, precision, tmp_path):
+def test_engine_matches_reference_engine(mods, oracle, precision, mode, tmp_path):
     e2e, eng = mods
     prompt = e2e.prompt_ids(32, seed=1)
     try:
@@ -30,7 +32,8 @@ def test_engine_matches_reference_engine(mods, oracle, precision, tmp_path):
                       warmup=0, repeat=1, logits_out=str(tmp_path / "r.bin"))
     except FileNotFoundError as err:
         pytest.skip(str(err))
-    e = eng.Engine(MODEL_DIR, precision, max_seq=256)
+    e = eng.Engine(MODEL_DIR, precision, max_seq=256, mode=mode)
+    assert e.mode == mode
     toks, _, _ = e.generate(prompt, 1)
     lg = oracle.bf16_to_f32(e.logits())
     lr = np.fromfile(tmp_path / "r.bin", np.float32)
@@ -39,16 +42,52 @@ def test_engine_matches_reference_engine(mods, oracle, precision, tmp_path):
     toks, ttft, dec = e.generate(prompt, 48)
     same = next((i for i, (a, b) in enumerate(zip(toks, ref["tokens"])) if a != b), 48)
     assert same >= 16, (same, toks[:20], ref["tokens"][:20])
+    assert e.device_status() == 0
     e.close()
 
 
-def test_graph_decode_is_deterministic_and_restartable(mods):
+@pytest.mark.parametrize("mode", ["persistent", "graph"])
+def test_decode_is_deterministic_and_restartable(mods, mode):
     e2e, eng = mods
-    e = eng.Engine(MODEL_DIR, "w8a16", max_seq=128)
+    e = eng.Engine(MODEL_DIR, "w8a16", max_seq=128, mode=mode)
     prompt = e2e.prompt_ids(20, seed=4)
     a, _, _ = e.generate(prompt, 40)
     b, _, _ = e.generate(prompt, 40)
     c, _, _ = e.generate(prompt[:10], 5)
     d, _, _ = e.generate(prompt, 40)
     assert a == b == d and len(c) == 5
+    assert e.device_status() == 0
+    e.close()
+
+
+def test_persistent_steps_split_across_calls(mods):
+    """Decoding in several persistent launches continues the same sequence
+    as one launch (token, position and output index carried on the device)."""
+    e2e, eng = mods
+    e = eng.Engine(MODEL_DIR, "w8a16", max_seq=128, mode="persistent")
+    prompt = e2e.prompt_ids(24, seed=5)
+    whole, _, _ = e.generate(prompt, 30)
+    import ctypes
+    from qwen25_b200 import ABI
+    arr = (ctypes.c_int * len(prompt))(*prompt)
+    assert ABI.b200_engine_prefill(e.handle, arr, len(prompt)) == 0
+    for n in (1, 7, 21):
+        assert ABI.b200_engine_decode(e.handle, n) == 0
+    out = (ctypes.c_int * 30)()
+    assert ABI.b200_engine_tokens(e.handle, out, 30) == 0
+    assert list(out) == whole
+    e.close()
+
+
+def test_decode_past_max_seq_is_rejected(mods):
+    e2e, eng = mods
+    import ctypes
+    from qwen25_b200 import ABI
+    e = eng.Engine(MODEL_DIR, "w8a16", max_seq=40)
+    prompt = e2e.prompt_ids(30, seed=6)
+    arr = (ctypes.c_int * len(prompt))(*prompt)
+    assert ABI.b200_engine_prefill(e.handle, arr, len(prompt)) == 0
+    assert ABI.b200_engine_decode(e.handle, 11) == -4  # B200_ERR_TOO_LARGE
+    assert ABI.b200_engine_decode(e.handle, 10) == 0
+    assert ABI.b200_engine_decode(e.handle, 1) == -4
     e.close()
