@@ -72,20 +72,23 @@ int b200_engine_decode(b200_engine_t engine, int steps);
 
 /* Decode modes.  PERSISTENT (the default where the shapes allow it): all
  * steps of one b200_engine_decode call in one cooperative kernel, one CTA
- * per SM, layers chained by grid-wide barriers while each CTA streams its
- * weight tiles ahead into shared memory.  GRAPH: one CUDA graph replay per
- * step (146 kernel launches for the 24-layer model). */
+ * per SM; each CTA streams its share of every weight matrix ahead into
+ * shared memory, and activations pass between CTAs as tagged words that are
+ * their own synchronisation.  GRAPH: one CUDA graph replay per step (146
+ * kernel launches for the 24-layer model). */
 #define B200_ENGINE_DECODE_PERSISTENT 0
 #define B200_ENGINE_DECODE_GRAPH 1
 /* Selects the decode mode (B200_ERR_TOO_LARGE: the persistent kernel does
  * not take this model's shapes / shared-memory needs). */
 int b200_engine_set_decode_mode(b200_engine_t engine, int mode);
-/* Profiling timeline of the persistent kernel: with barriers > 0 the next
- * decode calls record, for their first `barriers` grid barriers, each CTA's
- * arrival and release times (global timer, ns); 0 turns it off.  Allocates
- * a device buffer of grid x barriers x 16 bytes. */
-int b200_engine_set_trace(b200_engine_t engine, int barriers);
-/* Copies the timeline ([cta][barrier][arrive, leave]) to host memory when
+/* Profiling timeline of the persistent kernel: with phases > 0 the next
+ * decode calls record, for their first `phases` phases (5 per layer: q|k|v,
+ * attention, o_proj, gate|up, down_proj; then LM head, argmax), each CTA's
+ * input-staged, phase-done, first-weight-block-landed and input-arrived
+ * times (global timer, ns); 0 turns it off.  Allocates grid x phases x 32
+ * bytes. */
+int b200_engine_set_trace(b200_engine_t engine, int phases);
+/* Copies the timeline ([cta][phase][staged, done, block, arrived]) to host memory when
  * out != NULL (synchronises); returns the CTA count (0: tracing off). */
 int b200_engine_read_trace(b200_engine_t engine, unsigned long long* out);
 /* The current decode mode. */

@@ -50,7 +50,7 @@ typedef struct CUstream_st* b200_stream_t;
 #define B200_DEVICE_OK 0
 #define B200_DEVICE_TIMEOUT_PIPELINE 1 /* GEMM smem pipeline wait expired */
 #define B200_DEVICE_TIMEOUT_ACCUM 2    /* GEMM TMEM accumulator wait expired */
-#define B200_DEVICE_TIMEOUT_GRID 3     /* persistent decode: grid barrier wait expired */
+#define B200_DEVICE_TIMEOUT_GRID 3     /* persistent decode: wait for another CTA expired */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int b200_version(void);

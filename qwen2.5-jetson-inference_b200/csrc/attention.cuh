@@ -33,13 +33,13 @@ __host__ __device__ constexpr size_t attend_smem_floats(int seq_cap) {
 // rows [pos][64].  Positions [0, seq) are attended; position `cur` (or -1)
 // is taken from kcur / vcur (64 FP32 values in shared memory) instead of
 // the cache.  `sync()` synchronises the NT threads.  Thread `tid` < 64
-// writes out[tid].
-template <int NT, class Sync>
+// calls store(tid, output value of dimension tid).
+template <int NT, class Sync, class Store>
 __device__ __forceinline__ void attend_row(const float* qs, const bf16* kbase,
                                            const bf16* vbase, int seq, int cur,
                                            const float* kcur, const float* vcur,
                                            float* smem, int tid, Sync sync,
-                                           bf16* out) {
+                                           Store store) {
   constexpr int NW = NT / 32;
   float* scores = smem;
   float* red = smem + seq;
@@ -135,7 +135,7 @@ __device__ __forceinline__ void attend_row(const float* qs, const bf16* kbase,
       denom += red[w];
       o += part[w * kHeadDim + tid];
     }
-    out[tid] = __float2bfloat16_rn(o / denom);
+    store(tid, o / denom);
   }
   sync();  // smem reusable by the caller
 }

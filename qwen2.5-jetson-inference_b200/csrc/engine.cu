@@ -53,8 +53,10 @@ struct b200_engine {
   // persistent decode kernel (decode_persistent.cu)
   b200::PersistPlan plan;
   b200::PersistLayer* d_layers = nullptr;
-  unsigned* grid_words = nullptr;  // [0] barrier counter, [1] abort flag
+  unsigned* grid_words = nullptr;  // [0] abort flag
   int* d_status = nullptr;
+  unsigned long long* words = nullptr;  // tagged activations
+  unsigned epoch = 0;                   // tags used so far
   int mode = B200_ENGINE_DECODE_GRAPH;
   int h_pos = -1;  // position of the next decode step (-1: no prefill yet)
   unsigned long long* trace = nullptr;  // persistent-kernel timeline (optional)
@@ -196,9 +198,10 @@ attention_kernel(const bf16* __restrict__ qkv, int qkv_dim, const bf16* kcache,
   const bf16* q = qkv + size_t(t) * qkv_dim + head * hd;
   if (threadIdx.x < kHeadDim) qs[threadIdx.x] = __bfloat162float(q[threadIdx.x]);
   __syncthreads();
+  bf16* o = out + size_t(t) * heads * hd + head * hd;
   attend_row<128>(qs, kcache + size_t(kvh) * max_seq * hd, vcache + size_t(kvh) * max_seq * hd,
                   seq, -1, nullptr, nullptr, att_smem, threadIdx.x, [] { __syncthreads(); },
-                  out + size_t(t) * heads * hd + head * hd);
+                  [o](int d, float v) { o[d] = __float2bfloat16_rn(v); });
 }
 
 // Final argmax of the LM head (lowest index on ties) feeding the next step:
@@ -467,6 +470,18 @@ int b200_engine_create(b200_engine_t* out, const b200_engine_config* cfg,
   }
   e->plan = b200::plan_persistent(c.w8 != 0, c.hidden, c.intermediate, c.heads, c.kv_heads,
                                   c.vocab, c.max_seq);
+  if (e->plan.ok) {
+    const size_t bytes = b200::persist_words(c.layers, e->qkv_dim, c.hidden, c.intermediate,
+                                             e->plan.grid) * sizeof(unsigned long long);
+    err = cudaMalloc(&e->words, bytes);
+    if (err == cudaSuccess) err = cudaMemset(e->words, 0, bytes);
+    if (err != cudaSuccess) {
+      cudaGetLastError();
+      if (e->words) cudaFree(e->words);
+      e->words = nullptr;
+      e->plan.ok = false;
+    }
+  }
   e->mode = e->plan.ok ? B200_ENGINE_DECODE_PERSISTENT : B200_ENGINE_DECODE_GRAPH;
   *out = e;
   return B200_OK;
@@ -476,6 +491,7 @@ int b200_engine_destroy(b200_engine_t e) {
   if (e == nullptr) return B200_OK;
   if (e->graph) cudaGraphExecDestroy(e->graph);
   if (e->trace) cudaFree(e->trace);
+  if (e->words) cudaFree(e->words);
   cudaFree(e->arena);
   delete e;
   return B200_OK;
@@ -508,20 +524,20 @@ int b200_engine_set_decode_mode(b200_engine_t e, int mode) {
   return B200_OK;
 }
 
-int b200_engine_set_trace(b200_engine_t e, int barriers) {
-  if (e == nullptr || barriers < 0) return B200_ERR_INVALID_ARGUMENT;
+int b200_engine_set_trace(b200_engine_t e, int phases) {
+  if (e == nullptr || phases < 0) return B200_ERR_INVALID_ARGUMENT;
   if (e->trace) {
     ENGINE_TRY(check(cudaStreamSynchronize(e->stream)));
     cudaFree(e->trace);
     e->trace = nullptr;
     e->trace_count = 0;
   }
-  if (barriers == 0) return B200_OK;
+  if (phases == 0) return B200_OK;
   if (!e->plan.ok) return B200_ERR_TOO_LARGE;
-  const size_t bytes = size_t(e->plan.grid) * barriers * 2 * sizeof(unsigned long long);
+  const size_t bytes = size_t(e->plan.grid) * phases * 4 * sizeof(unsigned long long);
   ENGINE_TRY(check(cudaMalloc(&e->trace, bytes)));
   ENGINE_TRY(check(cudaMemset(e->trace, 0, bytes)));
-  e->trace_count = barriers;
+  e->trace_count = phases;
   return B200_OK;
 }
 
@@ -529,7 +545,7 @@ int b200_engine_read_trace(b200_engine_t e, unsigned long long* out) {
   if (e == nullptr) return B200_ERR_INVALID_ARGUMENT;
   if (e->trace == nullptr) return 0;
   if (out != nullptr) {
-    const size_t n = size_t(e->plan.grid) * e->trace_count * 2;
+    const size_t n = size_t(e->plan.grid) * e->trace_count * 4;
     ENGINE_TRY(check(cudaMemcpyAsync(out, e->trace, n * sizeof(unsigned long long),
                                      cudaMemcpyDeviceToHost, e->stream)));
     ENGINE_TRY(check(cudaStreamSynchronize(e->stream)));
@@ -575,26 +591,22 @@ int b200_engine_decode(b200_engine_t e, int steps) {
     a.theta = c.theta;
     a.embed = reinterpret_cast<const bf16*>(e->embed);
     a.final_norm = reinterpret_cast<const bf16*>(e->final_norm);
-    a.x = e->x;
-    a.qkv = e->qkv;
-    a.att = e->att;
-    a.gu = e->gu;
+    a.words = e->words;
+    a.epoch = e->epoch;
     a.logits = e->logits;
     a.kcache = e->kcache;
     a.vcache = e->vcache;
-    a.part_v = e->lm_value;
-    a.part_i = e->lm_index;
     a.d_token = e->d_token;
     a.d_pos = e->d_pos;
     a.d_step = e->d_step;
     a.d_out = e->d_out;
     a.max_out = c.max_seq;
-    a.grid_counter = e->grid_words;
-    a.grid_abort = reinterpret_cast<int*>(e->grid_words + 1);
+    a.grid_abort = reinterpret_cast<int*>(e->grid_words);
     a.status = e->d_status;
     a.trace = e->trace;
     a.trace_count = e->trace_count;
     a.steps = steps;
+    e->epoch += unsigned(steps);
     return check(b200::launch_persistent(c.w8 != 0, e->plan, a, e->stream));
   }
   if (e->graph == nullptr) {

@@ -134,17 +134,17 @@ class Engine:
                "engine_set_decode_mode")
 
     def trace(self, barriers: int) -> None:
-        """Records the persistent kernel's per-CTA barrier timeline for the
-        first `barriers` grid barriers of the next decode calls."""
+        """Records the persistent kernel's per-CTA phase timeline for the
+        first `barriers` phases of the next decode calls."""
         _check(ABI.b200_engine_set_trace(self.handle, barriers), "engine_set_trace")
         self._trace_barriers = barriers
 
     def read_trace(self) -> np.ndarray:
-        """[cta, barrier, (arrive, leave)] global-timer ns of the last decode."""
+        """[cta, phase, (staged, done, block landed, input arrived)] global-timer ns."""
         ctas = ABI.b200_engine_read_trace(self.handle, None)
         if ctas <= 0:
-            return np.zeros((0, 0, 2), np.uint64)
-        buf = np.zeros((ctas, self._trace_barriers, 2), np.uint64)
+            return np.zeros((0, 0, 4), np.uint64)
+        buf = np.zeros((ctas, self._trace_barriers, 4), np.uint64)
         rc = ABI.b200_engine_read_trace(self.handle, buf.ctypes.data)
         if rc < 0:
             _check(rc, "engine_read_trace")
