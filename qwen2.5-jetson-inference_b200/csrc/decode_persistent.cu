@@ -124,10 +124,7 @@ struct Spin {
   int n = 0;
 };
 __device__ __forceinline__ bool spin_on(Spin& s, const PersistArgs& a, const Smem& sm) {
-#ifndef B200_EXP_SLEEP
-#define B200_EXP_SLEEP 64
-#endif
-  __nanosleep(B200_EXP_SLEEP);  // eases the polling load on the L2 lines being written
+  __nanosleep(64);  // eases the polling load on the L2 lines being written
   if ((++s.n & 31) != 0) return true;
   if (*reinterpret_cast<volatile int*>(a.grid_abort) != 0 || *sm.abort_flag != 0) {
     *sm.abort_flag = 1;
@@ -152,6 +149,21 @@ __device__ __forceinline__ bool wait_word(const u64* p, unsigned tag, u64& w,
     w = ld_word(p);
     if (tag_of(w) == tag) return true;
     if (!spin_on(s, a, sm)) return false;
+  }
+}
+
+// Two tagged words, both loads issued before either tag is checked.
+__device__ __forceinline__ bool wait_word2(const u64* p0, const u64* p1, unsigned tag, u64& w0,
+                                           u64& w1, const PersistArgs& a, const Smem& sm) {
+  Spin s;
+  w0 = ld_word(p0);
+  w1 = ld_word(p1);
+  while (true) {
+    const bool h0 = tag_of(w0) == tag, h1 = tag_of(w1) == tag;
+    if (h0 && h1) return true;
+    if (!spin_on(s, a, sm)) return false;
+    if (!h0) w0 = ld_word(p0);
+    if (!h1) w1 = ld_word(p1);
   }
 }
 
@@ -449,43 +461,45 @@ __device__ __forceinline__ bool stage(const u64* words, const bf16* plain, unsig
 }
 
 // Products of one block with the staged vector.  Output o of the block is
-// row o (kPair: rows o and rows + o, the gate and up rows); kWPR warps per
-// output split the K chunks.  epi(o, vA, vB) runs on one lane per output.
-#ifdef B200_EXP_NOINLINE
-#define B200_GEMV_INLINE __noinline__
-#else
-#define B200_GEMV_INLINE __forceinline__
-#endif
-template <bool kW8, int kWPR, bool kPair, class Epi>
-__device__ B200_GEMV_INLINE void gemv_block(const unsigned char* blk, bool ok, int rows, int k,
+// row o (kPair: rows o and rows + o, the gate and up rows).  Each output is
+// computed by kLPR lanes of one warp (kWPR == 1, several outputs per warp)
+// or by kWPR whole warps (kLPR == 32, partials meet in shared memory); a
+// lane takes the 16-byte chunks c = first, first + kLPR * kWPR, ...
+// kK != 0 compiles the loop for that in_features (fully unrolled, every
+// chunk load issued up front); kK == 0 takes any in_features.
+// epi(o, vA, vB) runs on one lane per output.
+template <bool kW8, int kK, int kLPR, int kWPR, bool kPair, class Epi>
+__device__ __forceinline__ void gemv_block(const unsigned char* blk, bool ok, int rows, int k,
                                            Consumer& cs, const Smem& sm, int ct, Epi epi) {
+  static_assert(kWPR == 1 || kLPR == 32, "split outputs use whole warps");
   constexpr int kEPC = kW8 ? 16 : 8;
   constexpr int kPlanes = kEPC / 4;
-  constexpr int kGroups = kPWarps / kWPR;
-  constexpr int kSpan = 32 * kWPR;
+  constexpr int kRG = kWPR > 1 ? 1 : 32 / kLPR;               // outputs per warp
+  constexpr int kOutIt = kWPR > 1 ? kPWarps / kWPR : kPWarps * kRG;
+  constexpr int kSpan = kLPR * kWPR;                          // lanes per output
+  constexpr int kChunksK = kK / kEPC;
+  constexpr int kIt = kK != 0 ? (kChunksK + kSpan - 1) / kSpan : 0;
   const int lane = ct & 31, cw = ct >> 5;
-  const int rg = cw / kWPR, ksub = cw % kWPR;
+  const int ll = lane % kLPR;
+  const int ksub = kWPR > 1 ? cw % kWPR : 0;
+  const int slot = kWPR > 1 ? cw / kWPR : cw * kRG + lane / kLPR;
+  const int first = ksub * 32 + ll;
   const int row_bytes = kW8 ? k : 2 * k;
   const int groups = k >> 6;
-  const int chunks = k / kEPC;
+  const int chunks = kK != 0 ? kChunksK : k / kEPC;
   const int total_rows = kPair ? 2 * rows : rows;
   const bf16* sbase = reinterpret_cast<const bf16*>(blk + size_t(total_rows) * row_bytes);
-  const int iters = (rows + kGroups - 1) / kGroups;
+  const int iters = (rows + kOutIt - 1) / kOutIt;
   for (int it = 0; it < iters; ++it) {
-    const int o = rg + it * kGroups;
+    const int o = it * kOutIt + slot;
     const bool valid = ok && o < rows;
     float2 accA = f2(0.0f, 0.0f), accB = f2(0.0f, 0.0f);
-#ifdef B200_EXP_NOCOMPUTE
-    if (false) {
-#else
     if (valid) {
-#endif
       const unsigned char* wa = blk + size_t(o) * row_bytes;
       const unsigned char* wb = blk + size_t(o + rows) * row_bytes;
       const bf16* sa = sbase + o * groups;
       const bf16* sb = sbase + (o + rows) * groups;
-#pragma unroll 2
-      for (int c = ksub * 32 + lane; c < chunks; c += kSpan) {
+      auto body = [&](int c) {
         float4 xv[kPlanes];
 #pragma unroll
         for (int p = 0; p < kPlanes; ++p) xv[p] = sm.xs[p * chunks + c];
@@ -519,11 +533,21 @@ __device__ B200_GEMV_INLINE void gemv_block(const unsigned char* blk, bool ok, i
             accB = dot4_bf16_x2(vb.z, vb.w, xv[1], accB);
           }
         }
+      };
+      if constexpr (kK != 0) {
+#pragma unroll
+        for (int j = 0; j < kIt; ++j) {
+          const int c = first + j * kSpan;
+          if (kChunksK % kSpan == 0 || c < kChunksK) body(c);
+        }
+      } else {
+#pragma unroll 2
+        for (int c = first; c < chunks; c += kSpan) body(c);
       }
     }
     float vA = accA.x + accA.y, vB = accB.x + accB.y;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
+    for (int off = kLPR / 2; off > 0; off >>= 1) {
       vA += __shfl_xor_sync(0xffffffffu, vA, off);
       if constexpr (kPair) vB += __shfl_xor_sync(0xffffffffu, vB, off);
     }
@@ -545,25 +569,34 @@ __device__ B200_GEMV_INLINE void gemv_block(const unsigned char* blk, bool ok, i
       }
     }
     ++cs.red_it;
-    if (valid && ksub == 0 && lane == 0) epi(o, vA, vB);
+    if (valid && ksub == 0 && ll == 0) epi(o, vA, vB);
   }
 }
 
+// Lane mapping per block: enough lanes per output to use the 16 warps in
+// about one pass, compiled for the Qwen2.5-0.5B in_features (896 and 4864)
+// and generic otherwise.
 template <bool kW8, bool kPair, class Epi>
 __device__ __forceinline__ void gemv_any(const unsigned char* blk, bool ok, int rows, int k,
                                          Consumer& cs, const Smem& sm, int ct, Epi epi) {
-#ifdef B200_EXP_WPR2ONLY
-  gemv_block<kW8, 2, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
-  return;
-#endif
-  if (rows > 8) {
-    gemv_block<kW8, 1, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+  if (k == 896) {
+    if (rows > 32) {
+      gemv_block<kW8, 896, 8, 1, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+    } else if (rows > 16) {
+      gemv_block<kW8, 896, 16, 1, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+    } else {
+      gemv_block<kW8, 896, 32, 2, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+    }
+  } else if (k == 4864 && !kPair) {
+    gemv_block<kW8, 4864, 32, 2, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+  } else if (rows > 8) {
+    gemv_block<kW8, 0, 32, 1, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
   } else if (rows > 4) {
-    gemv_block<kW8, 2, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+    gemv_block<kW8, 0, 32, 2, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
   } else if (rows > 2) {
-    gemv_block<kW8, 4, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+    gemv_block<kW8, 0, 32, 4, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
   } else {
-    gemv_block<kW8, 8, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
+    gemv_block<kW8, 0, 32, 8, kPair>(blk, ok, rows, k, cs, sm, ct, epi);
   }
 }
 
@@ -574,9 +607,15 @@ __device__ __forceinline__ void gemv_any(const unsigned char* blk, bool ok, int 
 // positions are loaded into registers before the wait for this step's
 // q / k / v, so that the wait and the cache reads overlap.
 constexpr int kVPre = 16;  // V rows per warp held in registers
+__device__ __forceinline__ void trace_mark(const PersistArgs& a, int phase, int which, int ct) {
+  if (a.trace != nullptr && ct == 0 && phase < a.trace_count) {
+    a.trace[(size_t(blockIdx.x) * a.trace_count + phase) * 4 + which] = global_timer_ns();
+  }
+}
+
 __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem& sm,
                                                 const u64* qkv, u64* att, unsigned tag, int l,
-                                                int pos, int ct) {
+                                                int pos, int ct, int phase) {
   constexpr int NW = kPWarps;
   constexpr int half = kHeadDim / 2;
   const int h = blockIdx.x;
@@ -613,32 +652,20 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
     const int i = ct % half;
     const bool is_k = ct >= half;
     const int base = is_k ? (a.heads + kvh) * kHeadDim : h * kHeadDim;
-    u64 w0 = 0, w1 = 0;
-    wait_word(qkv + base + i, tag, w0, a, sm);
-    wait_word(qkv + base + i + half, tag, w1, a, sm);
-    const float x0 = bf16_lo(lo16(w0)), x1 = bf16_lo(lo16(w1));
     const float freq = powf(a.theta, -2.0f * float(i) / float(kHeadDim));
     float sn, cs;
     sincosf(float(pos) * freq, &sn, &cs);
-    const bf16 b0 = __float2bfloat16_rn(x0 * cs - x1 * sn);
-    const bf16 b1 = __float2bfloat16_rn(x1 * cs + x0 * sn);
-    r0 = __bfloat162float(b0);
-    r1 = __bfloat162float(b1);
-    if (is_k && writer) {
-      kc[size_t(pos) * kHeadDim + i] = b0;
-      kc[size_t(pos) * kHeadDim + i + half] = b1;
-      __threadfence();
-    }
+    u64 w0 = 0, w1 = 0;
+    wait_word2(qkv + base + i, qkv + base + i + half, tag, w0, w1, a, sm);
+    trace_mark(a, phase, 3, ct);
+    const float x0 = bf16_lo(lo16(w0)), x1 = bf16_lo(lo16(w1));
+    r0 = bf16_round(x0 * cs - x1 * sn);
+    r1 = bf16_round(x1 * cs + x0 * sn);
   } else if (ct < 2 * half + kHeadDim) {
     const int d = ct - 2 * half;
     u64 w = 0;
     wait_word(qkv + (a.heads + a.kv_heads + kvh) * kHeadDim + d, tag, w, a, sm);
-    const bf16 b0 = __ushort_as_bfloat16(static_cast<unsigned short>(lo16(w)));
-    r0 = __bfloat162float(b0);
-    if (writer) {
-      vc[size_t(pos) * kHeadDim + d] = b0;
-      __threadfence();
-    }
+    r0 = bf16_lo(lo16(w));
   }
   cbar();  // every warp is done with the previous phase's use of the region
   if (ct < 2 * half) {
@@ -650,14 +677,22 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
     vcur[ct - 2 * half] = r0;
   }
   if (cbar_or(*sm.abort_flag != 0)) return false;
-  // 3. scores, softmax
+  trace_mark(a, phase, 0, ct);
+  // 3. scores (q as float4 broadcasts, four independent partial sums),
+  //    softmax
   const float scale = rsqrtf(float(kHeadDim));
+  const float4* q4 = reinterpret_cast<const float4*>(qs);
   float mx = -FLT_MAX;
   for (int p = ct; p < seq; p += kPConsumers) {
-    float dot = 0.0f;
+    float2 d0 = f2(0.0f, 0.0f), d1 = f2(0.0f, 0.0f);
     if (p == pos) {
-#pragma unroll 16
-      for (int d = 0; d < kHeadDim; ++d) dot = fmaf(qs[d], kcur[d], dot);
+      const float4* k4 = reinterpret_cast<const float4*>(kcur);
+#pragma unroll
+      for (int c = 0; c < kHeadDim / 4; ++c) {
+        const float4 q = q4[c], kk = k4[c];
+        d0 = __ffma2_rn(f2(q.x, q.y), f2(kk.x, kk.y), d0);
+        d1 = __ffma2_rn(f2(q.z, q.w), f2(kk.z, kk.w), d1);
+      }
     } else {
       uint4 w[8];
       if (p == ct) {
@@ -670,17 +705,14 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        dot = fmaf(qs[8 * c + 0], bf16_lo(w[c].x), dot);
-        dot = fmaf(qs[8 * c + 1], bf16_hi(w[c].x), dot);
-        dot = fmaf(qs[8 * c + 2], bf16_lo(w[c].y), dot);
-        dot = fmaf(qs[8 * c + 3], bf16_hi(w[c].y), dot);
-        dot = fmaf(qs[8 * c + 4], bf16_lo(w[c].z), dot);
-        dot = fmaf(qs[8 * c + 5], bf16_hi(w[c].z), dot);
-        dot = fmaf(qs[8 * c + 6], bf16_lo(w[c].w), dot);
-        dot = fmaf(qs[8 * c + 7], bf16_hi(w[c].w), dot);
+        const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
+        d0 = __ffma2_rn(f2(qa.x, qa.y), f2(bf16_lo(w[c].x), bf16_hi(w[c].x)), d0);
+        d1 = __ffma2_rn(f2(qa.z, qa.w), f2(bf16_lo(w[c].y), bf16_hi(w[c].y)), d1);
+        d0 = __ffma2_rn(f2(qb.x, qb.y), f2(bf16_lo(w[c].z), bf16_hi(w[c].z)), d0);
+        d1 = __ffma2_rn(f2(qb.z, qb.w), f2(bf16_lo(w[c].w), bf16_hi(w[c].w)), d1);
       }
     }
-    const float sc = dot * scale;
+    const float sc = ((d0.x + d0.y) + (d1.x + d1.y)) * scale;
     scores[p] = sc;
     mx = fmaxf(mx, sc);
   }
@@ -703,35 +735,38 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
   if (lane == 0) red[warp] = sum;
   cbar();
   // 4. P.V: warp w takes positions w, w + 16, ...; lane l dims 2l, 2l + 1
-  float a0 = 0.0f, a1 = 0.0f;
+  //    (two independent accumulator pairs)
+  float2 acc0 = f2(0.0f, 0.0f), acc1 = f2(0.0f, 0.0f);
 #pragma unroll
   for (int j = 0; j < kVPre; ++j) {
     const int p = warp + j * NW;
     if (p < seq) {
       const float pr = scores[p];
-      const float v0 = p == pos ? vcur[2 * lane] : bf16_lo(vr[j]);
-      const float v1 = p == pos ? vcur[2 * lane + 1] : bf16_hi(vr[j]);
-      a0 = fmaf(pr, v0, a0);
-      a1 = fmaf(pr, v1, a1);
+      const float2 v = p == pos ? f2(vcur[2 * lane], vcur[2 * lane + 1])
+                                : f2(bf16_lo(vr[j]), bf16_hi(vr[j]));
+      if (j & 1) {
+        acc1 = __ffma2_rn(f2(pr, pr), v, acc1);
+      } else {
+        acc0 = __ffma2_rn(f2(pr, pr), v, acc0);
+      }
     }
   }
   for (int p = warp + kVPre * NW; p < seq; p += NW) {
     const float pr = scores[p];
-    float v0, v1;
+    float2 v;
     if (p == pos) {
-      v0 = vcur[2 * lane];
-      v1 = vcur[2 * lane + 1];
+      v = f2(vcur[2 * lane], vcur[2 * lane + 1]);
     } else {
-      const uint32_t v = __ldcg(vrow + size_t(p) * half);
-      v0 = bf16_lo(v);
-      v1 = bf16_hi(v);
+      const uint32_t raw = __ldcg(vrow + size_t(p) * half);
+      v = f2(bf16_lo(raw), bf16_hi(raw));
     }
-    a0 = fmaf(pr, v0, a0);
-    a1 = fmaf(pr, v1, a1);
+    acc0 = __ffma2_rn(f2(pr, pr), v, acc0);
   }
+  const float a0 = acc0.x + acc1.x, a1 = acc0.y + acc1.y;
   part[warp * kHeadDim + 2 * lane] = a0;
   part[warp * kHeadDim + 2 * lane + 1] = a1;
   cbar();
+  trace_mark(a, phase, 2, ct);
   if (ct < kHeadDim) {
     float denom = 0.0f, o = 0.0f;
 #pragma unroll
@@ -740,6 +775,15 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
       o += part[w * kHeadDim + ct];
     }
     st_word(att + h * kHeadDim + ct, tag_word(__float2bfloat16_rn(o / denom), tag));
+  }
+  // The new position's k / v into the cache (read from the next step on).
+  // The fence orders the stores before every later output of this CTA, and
+  // so before every read of them.
+  if (writer && ct < 2 * kHeadDim) {
+    const float v = ct < kHeadDim ? kcur[ct] : vcur[ct - kHeadDim];
+    bf16* dst = ct < kHeadDim ? kc : vc;
+    dst[size_t(pos) * kHeadDim + (ct & (kHeadDim - 1))] = __float2bfloat16_rn(v);
+    __threadfence();
   }
   return true;
 }
@@ -862,12 +906,13 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const P
         ++phase;
         // ---- attention (CTA h: head h)
         if (int(blockIdx.x) < a.heads) {
-          if (!(alive = attention_phase(a, sm, w_qkv, w_att, tag, l, pos, ct))) break;
+          if (!(alive = attention_phase(a, sm, w_qkv, w_att, tag, l, pos, ct, phase))) break;
         }
         mark(1);
         ++phase;
         // ---- x += W_o att
-        if (!(alive = stage<kW8 ? 16 : 8>(w_att, nullptr, tag, H, nullptr, 0.0f, nullptr, a, sm, ct, phase))) {
+        if (!(alive = stage<kW8 ? 16 : 8>(w_att, nullptr, tag, H, nullptr, 0.0f, nullptr, a, sm,
+                                          ct, phase))) {
           break;
         }
         mark(0);
