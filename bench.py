@@ -384,12 +384,17 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
             runs = [eng.generate(prompt, new_tokens) for _ in range(repeat)]
             toks = runs[0][0]
             ref = tokens[("reference", prec, "custom")]
+            am, gaps = eng.teacher_forced(prompt, ref)
+            dis = [j for j in range(len(ref)) if am[j] != ref[j]]
             out["native_engine"].append({
                 "precision": prec, "decode_mode": mode,
                 "decode_tok_s": round(statistics.median(
                     (new_tokens - 1) * 1e3 / r[2] for r in runs), 1),
                 "ttft_ms": round(statistics.median(r[1] for r in runs), 3),
                 "token_identical_prefix_vs_reference_kernels": prefix(toks, ref),
+                "teacher_forced_vs_reference_kernels": {
+                    "steps": len(ref), "agree": len(ref) - len(dis),
+                    "disagree_gaps": [round(gaps[j], 5) for j in dis]},
                 "device_status": eng.device_status()})
             eng.close()
     cpu = e2e.run("reference", model, prompt, backend="cpu", precision="fp32",
@@ -505,12 +510,70 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def engine_trace(layers=24):
+    """Per-phase timeline of one persistent decode step (the first step of a
+    128-token generation after a 32-token prompt) on the seeded synthetic
+    24-layer Qwen2.5, W8A16, from the engine's phase trace (global timer):
+    medians over layers of the input-arrival latency after the producing
+    phase ends, the staging time and the compute time, plus the LM head."""
+    import importlib
+    import numpy as np
+    load_pkg()
+    e2e = importlib.import_module("qwen25_b200.e2e")
+    q = importlib.import_module("qwen25_b200.qbin")
+    eng_mod = importlib.import_module("qwen25_b200.engine")
+    d = e2e.ensure_model(f"/tmp/b200_e2e_qwen2_{layers}layer",
+                         dict(q.QWEN25_05B, num_hidden_layers=layers), seed=0)
+    e = eng_mod.Engine(d, "w8a16", max_seq=256, mode="persistent")
+    prompt = e2e.prompt_ids(32, seed=1)
+    nph = 5 * layers + 2
+    e.generate(prompt, 128)
+    e.trace(nph)
+    e.generate(prompt, 128)
+    tr = e.read_trace().astype(np.int64)
+    e.trace(0)
+    runs = [e.generate(prompt, 128) for _ in range(5)]
+    e.close()
+    us = lambda v: round(float(v) / 1e3, 3)
+    # columns: 0 staged, 1 done, 2 first weight block landed, 3 input arrived
+    done_max = tr[:, :, 1].max(axis=0)
+    out = {"case": "engine_trace", "layers": layers,
+           "decode_tok_s": round(statistics.median(127e3 / r[2] for r in runs), 1),
+           "step_us": us(tr[:, nph - 1, 1].max() - tr[:, 0, 0][tr[:, 0, 0] > 0].min()),
+           "phases": {}}
+    names = "qkv attention o_proj gate_up down_proj".split()
+    for i, name in enumerate(names):
+        cols = [5 * l + i for l in range(1, layers)]
+        lat, stg, cmp = [], [], []
+        for c in cols:
+            prev_end = done_max[c - 1]
+            have = tr[:, c, 3] > 0
+            work = tr[:, c, 2] > 0
+            if have.any():
+                lat.append(np.median(tr[have, c, 3] - prev_end))
+                stg.append(np.median(tr[have, c, 0] - tr[have, c, 3]))
+            start = 0 if name == "attention" else 2  # attention has no weight block
+            if work.any():
+                cmp.append(np.median(tr[work, c, 1] - tr[work, c, start]))
+        out["phases"][name] = {
+            "input_arrival_after_producer_us": us(np.median(lat)) if lat else None,
+            "staging_us": us(np.median(stg)) if stg else None,
+            "compute_us": us(np.median(cmp)) if cmp else None,
+            "phase_span_us": us(np.median([done_max[c] - done_max[c - 1] for c in cols]))}
+    lm = nph - 2
+    out["phases"]["lm_head"] = {"phase_span_us": us(done_max[lm] - done_max[lm - 1])}
+    print(json.dumps(out), flush=True)
+
+
 def run_case(args):
     """One kernel, `warmup` + `steps` launches, for ncu captures (no timing).
     `engine_w8` / `engine_bf16` (+ `_graph`): the native engine on a 4-layer
     synthetic Qwen2.5 (real widths), one prefill + `steps` decode steps in
     the persistent kernel (or as graph replays)."""
     torch.cuda.set_device(0)
+    if args.case == "engine_trace":
+        engine_trace()
+        return
     if args.case.startswith("engine"):
         import importlib
         load_pkg()
@@ -572,7 +635,9 @@ def main():
                     help="run only the prefill GEMM sweep (configs[2])")
     ap.add_argument("--case", default=None,
                     help="profiling mode: run only one kernel, `--steps` launches "
-                         "(gemv_w8, gemv_bf16, lm_head, gemm_w8, gemm_bf16)")
+                         "(gemv_w8, gemv_bf16, lm_head, gemm_w8, gemm_bf16), the engine "
+                         "(engine_w8, engine_bf16, + _graph) or the persistent decode "
+                         "timeline (engine_trace)")
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=151936)
     ap.add_argument("--k", type=int, default=896)

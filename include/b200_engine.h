@@ -98,6 +98,11 @@ int b200_engine_decode_mode(b200_engine_t engine);
  * it. */
 int b200_engine_device_status(b200_engine_t engine, int clear);
 
+/* Replaces the token the next decode step consumes (after a prefill or a
+ * decode call): teacher forcing, e.g. to follow another engine's tokens and
+ * compare logits step by step.  The output list keeps the engine's own
+ * argmax. */
+int b200_engine_force_token(b200_engine_t engine, int token);
 /* Copies the first `count` output tokens to host memory (synchronises). */
 int b200_engine_tokens(b200_engine_t engine, int* out, int count);
 

@@ -603,10 +603,9 @@ __device__ __forceinline__ void gemv_any(const unsigned char* blk, bool ok, int 
 // Attention of head blockIdx.x for the token at `pos` of layer `l`, with
 // RoPE (half-split pairs, frequency theta^(-2i/64)) of q and k and the
 // cache store of k / v at `pos` by the first head of each KV group.  Same
-// arithmetic as attend_row (attention.cuh); the cache rows of earlier
-// positions are loaded into registers before the wait for this step's
-// q / k / v, so that the wait and the cache reads overlap.
-constexpr int kVPre = 16;  // V rows per warp held in registers
+// arithmetic as attend_row (attention.cuh), FP32 partial sums in another
+// order.
+constexpr int kVPre = 8;  // V rows per warp loaded before the scores
 __device__ __forceinline__ void trace_mark(const PersistArgs& a, int phase, int which, int ct) {
   if (a.trace != nullptr && ct == 0 && phase < a.trace_count) {
     a.trace[(size_t(blockIdx.x) * a.trace_count + phase) * 4 + which] = global_timer_ns();
@@ -633,19 +632,7 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
   bf16* kc = a.kcache + cache_off;
   bf16* vc = a.vcache + cache_off;
   const bool writer = h % group == 0;
-  // 1. cache rows of earlier positions
-  uint4 kr[8];
-  const bool kpre = ct < pos;
-  const uint4* krow = reinterpret_cast<const uint4*>(kc + size_t(ct) * kHeadDim);
-#pragma unroll
-  for (int c = 0; c < 8; ++c) kr[c] = kpre ? __ldcg(krow + c) : make_uint4(0u, 0u, 0u, 0u);
   const uint32_t* vrow = reinterpret_cast<const uint32_t*>(vc) + lane;
-  uint32_t vr[kVPre];
-#pragma unroll
-  for (int j = 0; j < kVPre; ++j) {
-    const int p = warp + j * NW;
-    vr[j] = p < pos ? __ldcg(vrow + size_t(p) * half) : 0u;
-  }
   // 2. this step's q, k (rotated) and v
   float r0 = 0.0f, r1 = 0.0f;
   if (ct < 2 * half) {
@@ -678,6 +665,13 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
   }
   if (cbar_or(*sm.abort_flag != 0)) return false;
   trace_mark(a, phase, 0, ct);
+  // The first V rows of this warp, loaded before the scores are computed.
+  uint32_t vr[kVPre];
+#pragma unroll
+  for (int j = 0; j < kVPre; ++j) {
+    const int p = warp + j * NW;
+    vr[j] = p < pos ? __ldcg(vrow + size_t(p) * half) : 0u;
+  }
   // 3. scores (q as float4 broadcasts, four independent partial sums),
   //    softmax
   const float scale = rsqrtf(float(kHeadDim));
@@ -695,14 +689,9 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
       }
     } else {
       uint4 w[8];
-      if (p == ct) {
+      const uint4* r = reinterpret_cast<const uint4*>(kc + size_t(p) * kHeadDim);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) w[c] = kr[c];
-      } else {
-        const uint4* r = reinterpret_cast<const uint4*>(kc + size_t(p) * kHeadDim);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) w[c] = __ldcg(r + c);
-      }
+      for (int c = 0; c < 8; ++c) w[c] = __ldcg(r + c);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
@@ -777,13 +766,13 @@ __device__ __forceinline__ bool attention_phase(const PersistArgs& a, const Smem
     st_word(att + h * kHeadDim + ct, tag_word(__float2bfloat16_rn(o / denom), tag));
   }
   // The new position's k / v into the cache (read from the next step on).
-  // The fence orders the stores before every later output of this CTA, and
-  // so before every read of them.
+  // The storing threads fence at the start of the next stage, while they
+  // wait for its input anyway: that orders the stores before every later
+  // output of this CTA, and so before every read of them.
   if (writer && ct < 2 * kHeadDim) {
     const float v = ct < kHeadDim ? kcur[ct] : vcur[ct - kHeadDim];
     bf16* dst = ct < kHeadDim ? kc : vc;
     dst[size_t(pos) * kHeadDim + (ct & (kHeadDim - 1))] = __float2bfloat16_rn(v);
-    __threadfence();
   }
   return true;
 }
@@ -911,6 +900,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const P
         mark(1);
         ++phase;
         // ---- x += W_o att
+        if (int(blockIdx.x) < a.heads && int(blockIdx.x) % (a.heads / a.kv_heads) == 0 &&
+            ct < 2 * kHeadDim) {
+          __threadfence();  // KV-cache stores of the attention phase
+        }
         if (!(alive = stage<kW8 ? 16 : 8>(w_att, nullptr, tag, H, nullptr, 0.0f, nullptr, a, sm,
                                           ct, phase))) {
           break;

@@ -624,6 +624,13 @@ int b200_engine_decode(b200_engine_t e, int steps) {
   return B200_OK;
 }
 
+int b200_engine_force_token(b200_engine_t e, int token) {
+  if (e == nullptr || token < 0 || token >= e->cfg.vocab) return B200_ERR_INVALID_ARGUMENT;
+  if (e->h_pos < 0) return B200_ERR_INVALID_ARGUMENT;
+  return check(cudaMemcpyAsync(e->d_token, &token, sizeof(int), cudaMemcpyHostToDevice,
+                               e->stream));
+}
+
 int b200_engine_tokens(b200_engine_t e, int* out, int count) {
   if (e == nullptr || out == nullptr || count < 0 || count > e->cfg.max_seq) {
     return B200_ERR_INVALID_ARGUMENT;

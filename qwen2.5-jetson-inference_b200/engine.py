@@ -46,6 +46,7 @@ for _name, (_args, _res) in {
     "b200_engine_decode_mode": ([_p], _i),
     "b200_engine_device_status": ([_p, _i], _i),
     "b200_engine_set_trace": ([_p, _i], _i),
+    "b200_engine_force_token": ([_p, _i], _i),
     "b200_engine_read_trace": ([_p, _p], _i),
 }.items():
     _fn = getattr(ABI, _name)
@@ -167,6 +168,29 @@ class Engine:
         _check(ABI.b200_engine_tokens(self.handle, out, new_tokens), "engine_tokens")
         t2 = time.perf_counter()
         return list(out), (t1 - t0) * 1e3, (t2 - t1) * 1e3
+
+    def teacher_forced(self, prompt, tokens):
+        """Follows `tokens` (another engine's greedy output for `prompt`):
+        after the prefill and after each forced step, records this engine's
+        argmax and the gap between its two largest BF16 logits.  Returns
+        (argmax list, gap list), one entry per token of `tokens`."""
+        arr = (_i * len(prompt))(*prompt)
+        _check(ABI.b200_engine_prefill(self.handle, arr, len(prompt)), "engine_prefill")
+        am, gaps = [], []
+
+        def record():
+            lg = self.logits().astype(np.uint32) << 16
+            v = lg.view(np.float32)
+            top = np.argpartition(-v, 1)[:2]
+            a, b = sorted(v[top], reverse=True)
+            am.append(int(np.flatnonzero(v == a)[0]))
+            gaps.append(float(a - b))
+        record()
+        for t in tokens[:-1]:
+            _check(ABI.b200_engine_force_token(self.handle, int(t)), "engine_force_token")
+            _check(ABI.b200_engine_decode(self.handle, 1), "engine_decode")
+            record()
+        return am, gaps
 
     def logits(self) -> np.ndarray:
         buf = (ctypes.c_uint16 * self.config.vocab)()
