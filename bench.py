@@ -254,7 +254,8 @@ def gemm_sweep(b200, device, reps=10):
 
 def sharded_bench(b200, world, rank, device, reps=5):
     """column-sharded W8A16 GEMM (M=8192; K,N = 8192,28672 and
-    28672,8192) with the NCCL all-gather, and the vocabulary-sharded LM head
+    28672,8192) with the NCCL all-gather and in its fused form (epilogue
+    stores into every rank's window over NVLink), and the vocabulary-sharded LM head
     (896 -> 151936, M=1) with the cross-GPU argmax.  Device time, max over
     ranks; TFLOP/s counts the whole (unsharded) GEMM."""
     import importlib
@@ -283,8 +284,13 @@ def sharded_bench(b200, world, rank, device, reps=5):
         def local():
             b200.gemm_w8a16(q, s, 64, None, x, yl, m, nr, k)
 
+        win = sh.Window(comm, m * n * 2)
+
+        def fused():
+            sh.gemm_w8a16_p2p(comm, win, q, s, None, x, m, n, k)
+
         res = {"m": m, "k": k, "n": n}
-        for name, fn in (("sharded", full), ("local_gemm", local)):
+        for name, fn in (("sharded", full), ("fused_p2p", fused), ("local_gemm", local)):
             for _ in range(2):
                 fn()
             torch.cuda.synchronize()
@@ -298,7 +304,9 @@ def sharded_bench(b200, world, rank, device, reps=5):
             t = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
             res[name + "_ms"] = round(t * 1e3, 3)
         res["tflops"] = round(2.0 * m * n * k / (res["sharded_ms"] / 1e3) / 1e12, 1)
+        res["tflops_fused_p2p"] = round(2.0 * m * n * k / (res["fused_p2p_ms"] / 1e3) / 1e12, 1)
         out["gemm"].append(res)
+        win.close()
         del q, s, x, y, ws, yl
         torch.cuda.empty_cache()
     v, k = 151936, 896

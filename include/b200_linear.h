@@ -168,6 +168,36 @@ int b200_comm_init(b200_comm_t* comm, const void* unique_id, int nranks,
 int b200_comm_wrap(b200_comm_t* comm, void* nccl_comm, int nranks, int rank);
 int b200_comm_destroy(b200_comm_t comm);
 
+/* A symmetric window: `bytes` of device memory on every rank, each rank's
+ * buffer mapped into every other rank's process (CUDA IPC over NVLink).
+ * Collective over the communicator (every rank calls it with the same
+ * bytes); the IPC handles are exchanged with an NCCL all-gather on `stream`,
+ * which the call synchronises. */
+typedef struct b200_window* b200_window_t;
+int b200_window_create(b200_comm_t comm, size_t bytes, b200_stream_t stream,
+                       b200_window_t* window);
+/* This rank's buffer of the window (device pointer), or NULL. */
+void* b200_window_ptr(b200_window_t window);
+/* Unmaps the peers' buffers and frees this rank's buffer. */
+int b200_window_destroy(b200_window_t window);
+
+/* The fused form of b200_sharded_gemm_w8a16_allgather: the local
+ * tensor-core GEMM stores each output tile straight into the window of
+ * every rank (16-byte stores over NVLink from its epilogue, so the exchange
+ * overlaps the math tile by tile), then a 4-byte NCCL all-reduce on `stream`
+ * orders every rank's stores before what follows on any rank's stream.  On
+ * completion the window holds the full row-major Y[tokens, out_features] on
+ * every rank; the window must hold at least tokens x out_features BF16.
+ * No gather workspace and no layout copy.  Same arguments and limits
+ * otherwise. */
+int b200_sharded_gemm_w8a16_p2p(b200_comm_t comm, b200_window_t output,
+                                const int8_t* weight_shard,
+                                const uint16_t* scales_shard, int group_size,
+                                const uint16_t* bias_shard,
+                                const uint16_t* input, int tokens,
+                                int out_features, int in_features,
+                                b200_stream_t stream);
+
 /* Gather workspace of b200_sharded_gemm_w8a16_allgather: tokens x
  * out_features BF16 (the [P][tokens][out_features/P] slots). */
 size_t b200_sharded_gemm_workspace_bytes(int tokens, int out_features,

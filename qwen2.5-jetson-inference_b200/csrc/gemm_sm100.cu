@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(Cfg<kW8, kMSub, kBN>::kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_w,
                const bf16* __restrict__ scales, const bf16* __restrict__ bias,
-               bf16* __restrict__ out, int m, int n, int k, int ldc) {
+               bf16* __restrict__ out, int m, int n, int k, int ldc,
+               const PeerOuts peers) {
   using C = Cfg<kW8, kMSub, kBN>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -332,8 +333,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const bf162 h = __floats2bfloat162_rn(f0, f1);
                   packed[e] = *reinterpret_cast<const uint32_t*>(&h);
                 }
-                reinterpret_cast<uint4*>(dst)[v] =
-                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                const uint4 val = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                reinterpret_cast<uint4*>(dst)[v] = val;
+                for (int pi = 0; pi < peers.n; ++pi) {
+                  reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + peers.delta[pi])[v] = val;
+                }
               }
             } else {
 #pragma unroll
@@ -341,7 +345,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 if (col0 + j < n) {
                   float f = __uint_as_float(r[j]);
                   if (bias) f += __bfloat162float(bias[col0 + j]);
-                  dst[j] = __float2bfloat16_rn(f);
+                  const bf16 hv = __float2bfloat16_rn(f);
+                  dst[j] = hv;
+                  for (int pi = 0; pi < peers.n; ++pi) {
+                    reinterpret_cast<bf16*>(reinterpret_cast<char*>(dst) + peers.delta[pi])[j] = hv;
+                  }
                 }
               }
             }
@@ -351,6 +359,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       tc_fence_before();
       mbar_arrive(bar_acc_empty + 8 * buf);
     }
+    // Stores into other GPUs' memory are made visible system-wide before
+    // the kernel completes.
+    if (peers.n > 0) __threadfence_system();
   } else if (warp >= 8) {
     // ---------------------------------------------------------- dequantiser
     if constexpr (kW8) {
@@ -596,7 +607,8 @@ __global__ void __launch_bounds__(Cfg2<kW8>::kThreads, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
                 const bf16* __restrict__ scales, const bf16* __restrict__ bias,
-                bf16* __restrict__ out, int m, int n, int k, int ldc) {
+                bf16* __restrict__ out, int m, int n, int k, int ldc,
+                const PeerOuts peers) {
   using C = Cfg2<kW8>;
   extern __shared__ __align__(1024) unsigned char smem_raw2[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -814,7 +826,43 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
           mbar_arrive_remote(acc_empty_leader + 8 * buf);
         }
       }
+      // Peer copies of this CTA's 128 x 256 half tile, pushed after the
+      // accumulator is released (the MMAs of the next tile run meanwhile):
+      // warp q re-reads the 32 rows it just stored and sends each row as one
+      // 512-byte segment (16 bytes per lane) to every peer, so the NVLink
+      // writes are whole, contiguous lines rather than one 16-byte piece per
+      // row per lane.
+      if (peers.n > 0 && acc_ok) {
+        const int col0 = nb * C::kBN;
+        const int rbase = mb * 256 + int(rank) * 128 + q * 32;
+        if (vec_ok && col0 + C::kBN <= n) {
+          static_assert(C::kBN * 2 == 32 * 16, "one 16-byte piece per lane per row");
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const int row = rbase + rr;
+            if (row >= m) break;
+            uint4* src = reinterpret_cast<uint4*>(out + size_t(row) * ldc + col0) + lane;
+            const uint4 v = *src;
+            for (int pi = 0; pi < peers.n; ++pi) {
+              *reinterpret_cast<uint4*>(reinterpret_cast<char*>(src) + peers.delta[pi]) = v;
+            }
+          }
+        } else {
+          for (int rr = 0; rr < 32; ++rr) {
+            const int row = rbase + rr;
+            if (row >= m) break;
+            for (int c = lane; c < C::kBN && col0 + c < n; c += 32) {
+              bf16* src = out + size_t(row) * ldc + col0 + c;
+              const bf16 v = *src;
+              for (int pi = 0; pi < peers.n; ++pi) {
+                *reinterpret_cast<bf16*>(reinterpret_cast<char*>(src) + peers.delta[pi]) = v;
+              }
+            }
+          }
+        }
+      }
     }
+    if (peers.n > 0) __threadfence_system();
   } else if (warp >= 8) {
     // ---------------------------------------------------------- dequantiser
     if constexpr (kW8) {
@@ -986,7 +1034,7 @@ int sm_count() {
 template <bool kW8, int kMSub, int kBN>
 cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
                        const bf16* input, bf16* output, int m, int n, int k,
-                       int ldc, cudaStream_t stream) {
+                       int ldc, const PeerOuts& peers, cudaStream_t stream) {
   using C = Cfg<kW8, kMSub, kBN>;
   CUtensorMap tx, tw;
   if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
@@ -1008,14 +1056,14 @@ cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
   const int tiles = ((m + C::kBM - 1) / C::kBM) * ((n + kBN - 1) / kBN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, scales, bias,
-                                                        output, m, n, k, ldc);
+                                                        output, m, n, k, ldc, peers);
   return cudaGetLastError();
 }
 
 template <bool kW8>
 cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias,
                         const bf16* input, bf16* output, int m, int n, int k,
-                        int ldc, cudaStream_t stream) {
+                        int ldc, const PeerOuts& peers, cudaStream_t stream) {
   using C = Cfg2<kW8>;
   CUtensorMap tx, tw;
   if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
@@ -1049,7 +1097,7 @@ cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k, ldc);
+  return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k, ldc, peers);
 }
 
 bool aligned16(const void* p) {
@@ -1090,18 +1138,23 @@ Tile choose_tile(bool w8, int m, int n) {
 template <bool kW8>
 cudaError_t launch_tile(Tile t, const void* weight, const bf16* scales,
                         const bf16* bias, const bf16* input, bf16* output,
-                        int m, int n, int k, int ldc, cudaStream_t stream) {
+                        int m, int n, int k, int ldc, const PeerOuts& peers,
+                        cudaStream_t stream) {
   switch (t) {
     case Tile::kPair256x256:
-      return launch_pair<kW8>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+      return launch_pair<kW8>(weight, scales, bias, input, output, m, n, k, ldc, peers, stream);
     case Tile::k256x128:
-      return launch_cfg<kW8, 2, 128>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+      return launch_cfg<kW8, 2, 128>(weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                     stream);
     case Tile::k128x256:
-      return launch_cfg<kW8, 1, 256>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+      return launch_cfg<kW8, 1, 256>(weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                     stream);
     case Tile::k128x128:
-      return launch_cfg<kW8, 1, 128>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+      return launch_cfg<kW8, 1, 128>(weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                     stream);
     default:
-      return launch_cfg<kW8, 1, 64>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+      return launch_cfg<kW8, 1, 64>(weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                    stream);
   }
 }
 
@@ -1200,8 +1253,8 @@ dequant_w8_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ sca
 }
 
 cudaError_t gemm_w8_two_pass(const void* weight, const bf16* scales, const bf16* bias,
-                             const bf16* input, bf16* output, int m, int n, int k,
-                             const Scratch& sc, cudaStream_t stream) {
+                             const bf16* input, bf16* output, int m, int n, int k, int ldc,
+                             const PeerOuts& peers, const Scratch& sc, cudaStream_t stream) {
   const size_t row_bytes = size_t(k) * 2;
   int block = int(sc.bytes / row_bytes) / 256 * 256;
   if (block <= 0) return cudaErrorMemoryAllocation;
@@ -1220,7 +1273,7 @@ cudaError_t gemm_w8_two_pass(const void* weight, const bf16* scales, const bf16*
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     e = launch_tile<false>(choose_tile(false, m, nr), wb, nullptr, bias ? bias + n0 : nullptr,
-                           input, output + n0, m, nr, k, n, stream);
+                           input, output + n0, m, nr, k, ldc, peers, stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -1233,9 +1286,10 @@ cudaError_t reserve_gemm_scratch(size_t bytes) {
   return scratch_get(bytes == 0 ? kScratchCap : bytes, true, &sc);
 }
 
-cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
-                           const bf16* bias, const bf16* input, bf16* output,
-                           int m, int n, int k, cudaStream_t stream) {
+cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales,
+                                 const bf16* bias, const bf16* input, bf16* output,
+                                 int m, int n, int k, int ldc, const PeerOuts& peers,
+                                 cudaStream_t stream) {
   if (w8 && m >= kTwoPassMinTokens && !getenv("B200_GEMM_ONE_PASS")) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(stream, &cap);
@@ -1245,12 +1299,22 @@ cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
     // 256-row block of this K falls back to the one-pass kernel.
     if (scratch_get(kScratchCap, cap == cudaStreamCaptureStatusNone, &sc) == cudaSuccess &&
         sc.bytes / (size_t(k) * 2) >= 256) {
-      return gemm_w8_two_pass(weight, scales, bias, input, output, m, n, k, sc, stream);
+      return gemm_w8_two_pass(weight, scales, bias, input, output, m, n, k, ldc, peers, sc,
+                              stream);
     }
   }
   const Tile t = choose_tile(w8, m, n);
-  return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, n, stream)
-            : launch_tile<false>(t, weight, scales, bias, input, output, m, n, k, n, stream);
+  return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                stream)
+            : launch_tile<false>(t, weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                 stream);
+}
+
+cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
+                           const bf16* bias, const bf16* input, bf16* output,
+                           int m, int n, int k, cudaStream_t stream) {
+  return launch_gemm_tc_peers(w8, weight, scales, bias, input, output, m, n, k, n, PeerOuts{},
+                              stream);
 }
 
 }  // namespace b200

@@ -44,12 +44,25 @@ cudaError_t launch_gemm_simt(bool w8, const void* weight, const bf16* scales,
                              const bf16* bias, const bf16* input, bf16* output,
                              int m, int n, int k, cudaStream_t stream);
 
+// Extra destinations of a GEMM's output tiles: the same tile is stored at
+// out + delta[i] bytes for each i < n (the output buffers of the other GPUs
+// of a node, mapped into this process), with plain 16-byte stores.
+struct PeerOuts {
+  long long delta[7] = {0, 0, 0, 0, 0, 0, 0};
+  int n = 0;
+};
+
 // gemm_sm100.cu: tcgen05 + TMA + TMEM path.
 bool gemm_tc_supported(bool w8, const void* weight, const void* input,
                        const void* output, int m, int n, int k);
 cudaError_t launch_gemm_tc(bool w8, const void* weight, const bf16* scales,
                            const bf16* bias, const bf16* input, bf16* output,
                            int m, int n, int k, cudaStream_t stream);
+// Same with an output row stride (ldc, elements) and peer destinations.
+cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales,
+                                 const bf16* bias, const bf16* input, bf16* output,
+                                 int m, int n, int k, int ldc, const PeerOuts& peers,
+                                 cudaStream_t stream);
 
 // Allocates (once per device) the BF16 weight buffer of the two-pass W8A16
 // prefill path; bytes == 0 means the default cap.

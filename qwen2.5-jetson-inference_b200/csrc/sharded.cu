@@ -6,6 +6,10 @@
 //    buffer [P][M][N/P], an in-place ncclAllGather fills the other slots over
 //    NVLink, and a copy kernel lays the slots out as the row-major [M, N]
 //    output the engine expects.
+//    The fused form (b200_sharded_gemm_w8a16_p2p) has no NCCL data path: the
+//    GEMM epilogue stores every output tile into the window buffer of every
+//    rank (CUDA IPC mappings, 16-byte stores over NVLink), at its final
+//    [M, N] position, while the next tiles are computed.
 //  * LM head: rank r owns vocabulary rows [r*V/P, (r+1)*V/P).  The local
 //    fused GEMV + argmax yields (BF16 logit, global index); it is packed into
 //    a 64-bit key that orders by value and then by lower index,
@@ -21,6 +25,7 @@
 #include <climits>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "b200_linear.h"
 #include "common.cuh"
@@ -31,6 +36,15 @@ struct b200_comm {
   int nranks = 1;
   int rank = 0;
   bool owned = false;
+};
+
+struct b200_window {
+  void* local = nullptr;
+  size_t bytes = 0;
+  int nranks = 1;
+  int rank = 0;
+  void* peer[8] = {};  // peer[r]: rank r's buffer in this process
+  int* token = nullptr;  // 4-byte operand of the ordering all-reduce
 };
 
 namespace b200 {
@@ -176,6 +190,138 @@ int b200_comm_destroy(b200_comm_t comm) {
   }
   delete comm;
   return rc;
+}
+
+int b200_window_create(b200_comm_t comm, size_t bytes, b200_stream_t stream,
+                       b200_window_t* out) {
+  if (comm == nullptr || out == nullptr || bytes == 0 || comm->nranks > 8) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  auto* w = new (std::nothrow) b200_window;
+  if (w == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  w->bytes = bytes;
+  w->nranks = comm->nranks;
+  w->rank = comm->rank;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto fail = [&](int rc) {
+    for (int r = 0; r < w->nranks; ++r) {
+      if (r != w->rank && w->peer[r] != nullptr) cudaIpcCloseMemHandle(w->peer[r]);
+    }
+    if (w->local) cudaFree(w->local);
+    if (w->token) cudaFree(w->token);
+    delete w;
+    return rc;
+  };
+  cudaError_t e = cudaMalloc(&w->local, bytes);
+  if (e != cudaSuccess) {
+    w->local = nullptr;
+    return fail(int(e));
+  }
+  w->peer[w->rank] = w->local;
+  e = cudaMalloc(&w->token, sizeof(int));
+  if (e != cudaSuccess) {
+    w->token = nullptr;
+    return fail(int(e));
+  }
+  if (w->nranks > 1) {
+    cudaIpcMemHandle_t mine;
+    e = cudaIpcGetMemHandle(&mine, w->local);
+    if (e != cudaSuccess) return fail(int(e));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    void* dev = nullptr;
+    e = cudaMalloc(&dev, hb * w->nranks);
+    if (e != cudaSuccess) return fail(int(e));
+    std::vector<cudaIpcMemHandle_t> all(w->nranks);
+    e = cudaMemcpyAsync(static_cast<char*>(dev) + hb * w->rank, &mine, hb,
+                        cudaMemcpyHostToDevice, s);
+    int rc = e == cudaSuccess ? B200_OK : int(e);
+    if (rc == B200_OK) {
+      rc = b200::nccl_status(ncclAllGather(static_cast<char*>(dev) + hb * w->rank, dev, hb,
+                                           ncclUint8, comm->nccl, s));
+    }
+    if (rc == B200_OK) {
+      e = cudaMemcpyAsync(all.data(), dev, hb * w->nranks, cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+      rc = e == cudaSuccess ? B200_OK : int(e);
+    }
+    cudaFree(dev);
+    if (rc != B200_OK) return fail(rc);
+    for (int r = 0; r < w->nranks; ++r) {
+      if (r == w->rank) continue;
+      e = cudaIpcOpenMemHandle(&w->peer[r], all[r], cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        w->peer[r] = nullptr;
+        return fail(int(e));
+      }
+    }
+  }
+  *out = w;
+  return B200_OK;
+}
+
+void* b200_window_ptr(b200_window_t w) { return w == nullptr ? nullptr : w->local; }
+
+int b200_window_destroy(b200_window_t w) {
+  if (w == nullptr) return B200_OK;
+  cudaError_t first = cudaSuccess;
+  for (int r = 0; r < w->nranks; ++r) {
+    if (r != w->rank && w->peer[r] != nullptr) {
+      const cudaError_t e = cudaIpcCloseMemHandle(w->peer[r]);
+      if (first == cudaSuccess) first = e;
+    }
+  }
+  cudaError_t e = cudaFree(w->local);
+  if (first == cudaSuccess) first = e;
+  e = cudaFree(w->token);
+  if (first == cudaSuccess) first = e;
+  delete w;
+  return first == cudaSuccess ? B200_OK : int(first);
+}
+
+int b200_sharded_gemm_w8a16_p2p(b200_comm_t comm, b200_window_t out,
+                                const int8_t* weight_shard, const uint16_t* scales_shard,
+                                int group_size, const uint16_t* bias_shard,
+                                const uint16_t* input, int tokens, int out_features,
+                                int in_features, b200_stream_t stream) {
+  if (group_size != 64) return B200_ERR_GROUP_SIZE;
+  if (comm == nullptr || out == nullptr || tokens < 0 || out_features < 0 ||
+      in_features <= 0 || out->nranks != comm->nranks || out->rank != comm->rank) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  const int p = comm->nranks;
+  if (out_features % p != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int ns = out_features / p;
+  if (tokens == 0 || out_features == 0) return B200_OK;
+  if (ns % 8 != 0 || out_features % 8 != 0) return B200_ERR_INVALID_ARGUMENT;
+  if (weight_shard == nullptr || scales_shard == nullptr || input == nullptr) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  if (size_t(tokens) * size_t(out_features) * 2 > out->bytes) return B200_ERR_WORKSPACE;
+  if (!b200::gemm_tc_supported(true, weight_shard, input, out->local, tokens, ns,
+                               in_features)) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // This rank's columns of the row-major [tokens, out_features] output.
+  bf16* mine = static_cast<bf16*>(out->local) + size_t(comm->rank) * ns;
+  b200::PeerOuts peers;
+  for (int r = 0; r < p; ++r) {
+    if (r == comm->rank) continue;
+    peers.delta[peers.n++] =
+        static_cast<char*>(out->peer[r]) - static_cast<char*>(out->local);
+  }
+  cudaError_t e = b200::launch_gemm_tc_peers(
+      true, weight_shard, reinterpret_cast<const bf16*>(scales_shard),
+      reinterpret_cast<const bf16*>(bias_shard), reinterpret_cast<const bf16*>(input), mine,
+      tokens, ns, in_features, out_features, peers, s);
+  if (e != cudaSuccess) return int(e);
+  if (p > 1) {
+    // Ordering point: a rank passes this all-reduce only after every rank's
+    // GEMM (and so its stores into this rank's window) has completed.
+    return b200::nccl_status(
+        ncclAllReduce(out->token, out->token, 1, ncclInt32, ncclSum, comm->nccl, s));
+  }
+  return B200_OK;
 }
 
 size_t b200_sharded_gemm_workspace_bytes(int tokens, int out_features,

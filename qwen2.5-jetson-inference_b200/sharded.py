@@ -3,7 +3,8 @@
 Mirrors the C ABI of include/b200_linear.h (b200_comm_*, b200_sharded_*):
 an NCCL communicator is created from a unique id that rank 0 makes and the
 other ranks receive through ``torch.distributed`` (any backend, gloo
-included), then the sharded W8A16 GEMM (+ NCCL all-gather) and the
+included), then the sharded W8A16 GEMM (+ NCCL all-gather, or fused with
+the exchange through a symmetric window of NVLink-mapped buffers) and the
 vocabulary-sharded LM head (+ cross-GPU argmax) run on each rank's stream.
 The reference is single-GPU; these are the sharded forms of its gemm_w8a16
 and lm_head_bf16 (src/cuda/kernels.cu:1566-1579, 1657-1684).
@@ -29,6 +30,10 @@ for _name, (_args, _res) in {
     "b200_sharded_gemm_w8a16_allgather": (
         [_p, _p, _p, _i, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "b200_sharded_lm_head_workspace_bytes": ([_i, _i], ctypes.c_size_t),
+    "b200_window_create": ([_p, ctypes.c_size_t, _p, ctypes.POINTER(_p)], _i),
+    "b200_window_ptr": ([_p], _p),
+    "b200_window_destroy": ([_p], _i),
+    "b200_sharded_gemm_w8a16_p2p": ([_p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _p], _i),
     "b200_sharded_lm_head_bf16": ([_p, _p, _p, _p, _p, _p, _p, _i, _i, _p], _i),
 }.items():
     _fn = getattr(ABI, _name)
@@ -99,6 +104,60 @@ def gemm_w8a16_allgather(comm: Comm, weight_shard, scales_shard, bias_shard, inp
         comm.handle, _ptr(weight_shard), _ptr(scales_shard), 64, _ptr(bias_shard),
         _ptr(input), _ptr(output), _ptr(workspace), tokens, out_features, in_features,
         _stream(stream)), "sharded_gemm_w8a16_allgather")
+
+
+class Window:
+    """A symmetric device buffer: `nbytes` on every rank, every rank's buffer
+    mapped into every process (collective over `comm`)."""
+
+    def __init__(self, comm: Comm, nbytes: int, stream=None):
+        self.handle = _p()
+        self.nbytes = nbytes
+        _check(ABI.b200_window_create(comm.handle, nbytes, _stream(stream),
+                                      ctypes.byref(self.handle)), "window_create")
+
+    def ptr(self) -> int:
+        return ABI.b200_window_ptr(self.handle)
+
+    def tensor(self, shape, dtype=torch.bfloat16, device=None):
+        """This rank's buffer viewed as a tensor (no copy; valid while open)."""
+        n = 1
+        for d in shape:
+            n *= d
+        itemsize = torch.empty((), dtype=dtype).element_size()
+        if n * itemsize > self.nbytes:
+            raise ValueError("shape exceeds the window")
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+
+        class _Iface:  # __cuda_array_interface__ view of the raw pointer
+            pass
+        iface = _Iface()
+        typestr = {torch.bfloat16: "<f2", torch.float16: "<f2", torch.float32: "<f4",
+                   torch.int32: "<i4", torch.uint8: "|u1"}[dtype]
+        iface.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                          "data": (self.ptr(), False), "version": 3}
+        t = torch.as_tensor(iface, device=dev)
+        return t.view(dtype) if dtype == torch.bfloat16 else t
+
+    def close(self):
+        if self.handle:
+            _check(ABI.b200_window_destroy(self.handle), "window_destroy")
+            self.handle = _p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def gemm_w8a16_p2p(comm: Comm, window: Window, weight_shard, scales_shard, bias_shard,
+                   input, tokens, out_features, in_features, stream=None):
+    """Fused sharded GEMM + all-gather: the full Y lands in every rank's window."""
+    _check(ABI.b200_sharded_gemm_w8a16_p2p(
+        comm.handle, window.handle, _ptr(weight_shard), _ptr(scales_shard), 64,
+        _ptr(bias_shard), _ptr(input), tokens, out_features, in_features,
+        _stream(stream)), "sharded_gemm_w8a16_p2p")
 
 
 def gemm_workspace(tokens, out_features, nranks, device=None):

@@ -1,6 +1,7 @@
 """One rank of the multi-GPU sharded-Linear check (launched by torchrun from
 tests/test_sharded_gpu.py).  Every rank builds the same seeded full weights,
-keeps its shard, runs the sharded W8A16 GEMM + all-gather and the
+keeps its shard, runs the sharded W8A16 GEMM + all-gather, its fused form
+(tiles stored into every rank's window over NVLink) and the
 vocabulary-sharded LM head, and compares with the single-GPU kernels on the
 full matrices.  Exit code 0 = all checks passed."""
 import os
@@ -45,6 +46,33 @@ def main():
     tol = ref.float().abs() * 2.0 ** -7 * 1.01 + 1e-4
     if not bool((diff <= tol).all()):
         failures.append(f"gemm max diff {diff.max().item()}")
+    # --- the fused form: tiles stored into every rank's window by the GEMM
+    win = sh.Window(comm, m * n * 2)
+    sh.gemm_w8a16_p2p(comm, win, q[r0:r0 + nr].contiguous(), s[r0:r0 + nr].contiguous(),
+                      bias[r0:r0 + nr].contiguous(), x, m, n, k)
+    torch.cuda.synchronize()
+    yw = win.tensor((m, n)).clone()
+    if not torch.equal(yw, y):
+        failures.append(f"p2p gemm differs from all-gather: max "
+                        f"{(yw.float() - y.float()).abs().max().item()}")
+    # two-pass path (tokens >= 1024), bias-free, and a second call on the
+    # same window
+    m2 = 1024
+    x2 = torch.randn(m2, k, generator=g, device=dev).to(torch.bfloat16)
+    win2 = sh.Window(comm, m2 * n * 2)
+    for _ in range(2):
+        sh.gemm_w8a16_p2p(comm, win2, q[r0:r0 + nr].contiguous(), s[r0:r0 + nr].contiguous(),
+                          None, x2, m2, n, k)
+    ref2 = torch.empty(m2, n, dtype=torch.bfloat16, device=dev)
+    b200.gemm_w8a16(q, s, 64, None, x2, ref2, m2, n, k)
+    torch.cuda.synchronize()
+    y2 = win2.tensor((m2, n)).clone()
+    d2 = (y2.float() - ref2.float()).abs()
+    tol2 = ref2.float().abs() * 2.0 ** -7 * 1.01 + 1e-4
+    if not bool((d2 <= tol2).all()):
+        failures.append(f"p2p gemm (two-pass) max diff {d2.max().item()}")
+    win.close()
+    win2.close()
     # --- vocabulary-sharded LM head with a tie across the shard boundary
     v, kk = 4096 * world, 896
     wl = (torch.randn(v, kk, generator=g, device=dev) * 0.02).to(torch.bfloat16)

@@ -50,6 +50,30 @@ def test_single_rank_comm_matches_unsharded(b200, sh, cuda):
     comm.close()
 
 
+
+def test_single_rank_window_gemm_matches_unsharded(b200, sh, cuda):
+    """The fused form on one rank: the window holds Y, bit-identical to the
+    plain GEMM (same tiles; the peer list is empty)."""
+    import torch
+    comm = sh.Comm(sh.new_unique_id(), 1, 0)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(6)
+    for m, k, n in ((300, 896, 4864), (1024, 896, 1024)):
+        w = torch.randn(n, k, generator=g, device=cuda) * 0.02
+        q, s = b200.quantize_groupwise(w)
+        bias = (torch.randn(n, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+        x = torch.randn(m, k, generator=g, device=cuda).to(torch.bfloat16)
+        win = sh.Window(comm, m * n * 2)
+        sh.gemm_w8a16_p2p(comm, win, q, s, bias, x, m, n, k)
+        ref = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+        b200.gemm_w8a16(q, s, 64, bias, x, ref, m, n, k)
+        torch.cuda.synchronize()
+        assert torch.equal(win.tensor((m, n)), ref)
+        with pytest.raises(Exception):
+            sh.gemm_w8a16_p2p(comm, win, q, s, bias, x, m + 1, n, k)  # window too small
+        win.close()
+    comm.close()
+
 def test_sharded_rejects_bad_splits(b200, sh, cuda):
     import torch
     comm = sh.Comm(sh.new_unique_id(), 1, 0)
