@@ -220,8 +220,12 @@ size_t b200_sharded_lm_head_workspace_bytes(int vocab, int nranks);
 /* Vocabulary-sharded fused LM head: this rank holds vocabulary rows
  * [rank*V/P, (rank+1)*V/P) and writes their BF16 logits to logits_shard;
  * every rank receives in *argmax the global index of the largest BF16 logit,
- * lowest index on ties (one NCCL max all-reduce of a packed 64-bit key).
- * vocab must be a multiple of nranks. */
+ * lowest index on ties.  With P > 1 the ranks exchange packed 64-bit keys
+ * through a small window of NVLink-mapped slots that the communicator
+ * creates on the first call (collective and synchronising: not inside a
+ * stream capture the first time); one kernel per rank publishes its key and
+ * reduces all P (bounded wait; an expired wait is reported by
+ * b200_device_status).  vocab must be a multiple of nranks. */
 int b200_sharded_lm_head_bf16(b200_comm_t comm, const uint16_t* weight_shard,
                               const uint16_t* bias_shard,
                               const uint16_t* input, uint16_t* logits_shard,

@@ -9,6 +9,7 @@
 namespace b200 {
 cudaError_t read_device_status(int* value, bool clear);  // gemm_sm100.cu
 cudaError_t read_gemv_status(int* value, bool clear);    // gemv.cu
+cudaError_t read_comm_status(int* value, bool clear);    // sharded.cu
 }
 
 using b200::bf16;
@@ -120,11 +121,12 @@ const char* b200_status_string(int status) {
 }
 
 int b200_device_status(int clear) {
-  int gemm = 0, gemv = 0;
+  int gemm = 0, gemv = 0, comm = 0;
   cudaError_t e = b200::read_device_status(&gemm, clear != 0);  // synchronises
   if (e == cudaSuccess) e = b200::read_gemv_status(&gemv, clear != 0);
+  if (e == cudaSuccess) e = b200::read_comm_status(&comm, clear != 0);
   if (e != cudaSuccess) return -int(e);
-  return gemm != 0 ? gemm : gemv;
+  return gemm != 0 ? gemm : gemv != 0 ? gemv : comm;
 }
 
 int b200_gemv_bf16(const uint16_t* weight, const uint16_t* bias,

@@ -13,9 +13,11 @@
 //  * LM head: rank r owns vocabulary rows [r*V/P, (r+1)*V/P).  The local
 //    fused GEMV + argmax yields (BF16 logit, global index); it is packed into
 //    a 64-bit key that orders by value and then by lower index,
-//    (orderable(value) << 32) | (0xFFFFFFFF - index), so one
-//    ncclAllReduce(max) over P keys gives the global argmax with the
-//    reference's lowest-index tie rule (src/cuda/kernels.cu:545-603).
+//    (orderable(value) << 32) | (0xFFFFFFFF - index), so the largest of the
+//    P keys is the global argmax with the reference's lowest-index tie rule
+//    (src/cuda/kernels.cu:545-603).  With P > 1 one kernel per rank stores
+//    its key into every rank's slot window over NVLink and reduces the P
+//    keys of its own window (no collective call).
 //
 // The reference has no multi-GPU path; these are the sharded forms of its
 // gemm_w8a16 and lm_head_bf16 (src/cuda/kernels.cu:1566-1579, 1657-1684).
@@ -31,11 +33,15 @@
 #include "common.cuh"
 #include "kernels.h"
 
+struct b200_window;
+
 struct b200_comm {
   ncclComm_t nccl = nullptr;
   int nranks = 1;
   int rank = 0;
   bool owned = false;
+  b200_window* keys = nullptr;  // argmax exchange slots (created on first use)
+  unsigned long long seq = 0;   // exchanges so far (same on every rank)
 };
 
 struct b200_window {
@@ -127,9 +133,110 @@ __global__ void decode_argmax_key_kernel(const unsigned long long* __restrict__ 
   *argmax = k == 0ull ? 0 : int(0xFFFFFFFFull - (k & 0xFFFFFFFFull));
 }
 
+__device__ int g_comm_status = 0;
+
+// Cross-GPU argmax without a collective: reduces this rank's per-CTA
+// partials to a key, stores (key, seq) into slot `rank` of every rank's
+// window (NVLink stores: key, system fence, then the sequence number), waits
+// (bounded) until every slot of its own window carries `seq`, and decodes
+// the largest key.  One CTA per rank; waits end after kWaitTimeoutNs with
+// B200_DEVICE_TIMEOUT_GRID in g_comm_status.
+struct KeySlots {
+  unsigned long long* slot[8];  // rank q's window, as mapped in this process
+};
+
+__global__ void __launch_bounds__(256)
+exchange_argmax_kernel(const float* __restrict__ block_value,
+                       const int* __restrict__ block_index, int count, int index_offset,
+                       KeySlots windows, int nranks, int rank, unsigned long long seq,
+                       int* __restrict__ argmax) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ unsigned long long keys[8];
+  pdl_wait_primary();
+  float best = -FLT_MAX;
+  int best_index = INT_MAX;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    if (better(block_value[i], block_index[i], best, best_index)) {
+      best = block_value[i];
+      best_index = block_index[i];
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_index, off);
+    if (better(ov, oi, best, best_index)) {
+      best = ov;
+      best_index = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = best_index;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) {
+      if (better(sv[w], si[w], b, bi)) {
+        b = sv[w];
+        bi = si[w];
+      }
+    }
+    unsigned long long k = 0ull;
+    if (bi != INT_MAX) {
+      const unsigned int gi = unsigned(bi + index_offset);
+      k = (static_cast<unsigned long long>(float_order_key(b)) << 32) | (0xFFFFFFFFull - gi);
+    }
+    // slot layout per window: [rank][key, seq]
+    for (int q = 0; q < nranks; ++q) {
+      volatile unsigned long long* dst = windows.slot[q] + 2 * rank;
+      dst[0] = k;
+    }
+    __threadfence_system();
+    for (int q = 0; q < nranks; ++q) {
+      volatile unsigned long long* dst = windows.slot[q] + 2 * rank;
+      dst[1] = seq;
+    }
+  }
+  if (threadIdx.x < nranks) {
+    volatile unsigned long long* mine = windows.slot[rank] + 2 * threadIdx.x;
+    const uint64_t start = global_timer_ns();
+    unsigned long long k = 0ull;
+    while (true) {
+      if (mine[1] == seq) {
+        __threadfence_system();
+        k = mine[0];
+        break;
+      }
+      if (global_timer_ns() - start > kWaitTimeoutNs) {
+        atomicCAS(&g_comm_status, 0, B200_DEVICE_TIMEOUT_GRID);
+        break;
+      }
+    }
+    keys[threadIdx.x] = k;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long k = 0ull;
+    for (int q = 0; q < nranks; ++q) k = keys[q] > k ? keys[q] : k;
+    *argmax = k == 0ull ? 0 : int(0xFFFFFFFFull - (k & 0xFFFFFFFFull));
+  }
+}
+
 int nccl_status(ncclResult_t r) { return r == ncclSuccess ? B200_OK : B200_ERR_NCCL; }
 
 }  // namespace
+
+cudaError_t read_comm_status(int* value, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_comm_status, sizeof(int));
+  if (e != cudaSuccess || !clear) return e;
+  const int zero = 0;
+  return cudaMemcpyToSymbol(g_comm_status, &zero, sizeof(int));
+}
+
 }  // namespace b200
 
 using b200::bf16;
@@ -184,9 +291,11 @@ int b200_comm_wrap(b200_comm_t* comm, void* nccl_comm, int nranks, int rank) {
 
 int b200_comm_destroy(b200_comm_t comm) {
   if (comm == nullptr) return B200_OK;
-  int rc = B200_OK;
+  int rc = b200_window_destroy(comm->keys);
+  comm->keys = nullptr;
   if (comm->owned && comm->nccl != nullptr) {
-    rc = b200::nccl_status(ncclCommDestroy(comm->nccl));
+    const int r2 = b200::nccl_status(ncclCommDestroy(comm->nccl));
+    if (rc == B200_OK) rc = r2;
   }
   delete comm;
   return rc;
@@ -218,6 +327,8 @@ int b200_window_create(b200_comm_t comm, size_t bytes, b200_stream_t stream,
     return fail(int(e));
   }
   w->peer[w->rank] = w->local;
+  e = cudaMemsetAsync(w->local, 0, bytes, s);
+  if (e != cudaSuccess) return fail(int(e));
   e = cudaMalloc(&w->token, sizeof(int));
   if (e != cudaSuccess) {
     w->token = nullptr;
@@ -405,15 +516,39 @@ int b200_sharded_lm_head_bf16(b200_comm_t comm, const uint16_t* weight_shard,
       shard, in_features, block_value, block_index, stream, &grid);
   if (e != cudaSuccess) return int(e);
   if (grid > blocks) return B200_ERR_WORKSPACE;
+  if (p > 1) {
+    // Cross-GPU argmax through the key window (created on the first call,
+    // collectively: every rank makes the same sequence of calls).
+    if (comm->keys == nullptr) {
+      const int rc = b200_window_create(comm, 2 * 8 * sizeof(unsigned long long), stream,
+                                        &comm->keys);
+      if (rc != B200_OK) return rc;
+    }
+    b200::KeySlots slots;
+    for (int q = 0; q < 8; ++q) {
+      slots.slot[q] = static_cast<unsigned long long*>(q < p ? comm->keys->peer[q] : nullptr);
+    }
+    ++comm->seq;
+    // Programmatic dependent launch: the exchange kernel is resident before
+    // the GEMV finishes and waits for it in griddepcontrol.wait.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, b200::exchange_argmax_kernel, (const float*)block_value,
+                           (const int*)block_index, grid, comm->rank * shard, slots, p,
+                           comm->rank, comm->seq, argmax);
+    return e == cudaSuccess ? B200_OK : int(e);
+  }
   b200::local_argmax_key_kernel<<<1, 1024, 0, stream>>>(
       block_value, block_index, grid, comm->rank * shard, key);
   e = cudaGetLastError();
   if (e != cudaSuccess) return int(e);
-  if (p > 1) {
-    const int rc = b200::nccl_status(
-        ncclAllReduce(key, key, 1, ncclUint64, ncclMax, comm->nccl, stream));
-    if (rc != B200_OK) return rc;
-  }
   b200::decode_argmax_key_kernel<<<1, 1, 0, stream>>>(key, argmax);
   e = cudaGetLastError();
   return e == cudaSuccess ? B200_OK : int(e);
