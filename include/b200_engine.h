@@ -91,6 +91,14 @@ int b200_engine_set_trace(b200_engine_t engine, int phases);
 /* Copies the timeline ([cta][phase][staged, done, block, arrived]) to host memory when
  * out != NULL (synchronises); returns the CTA count (0: tracing off). */
 int b200_engine_read_trace(b200_engine_t engine, unsigned long long* out);
+/* Test hook of the failure path (persistent mode): in the next decode call,
+ * CTA 0 stops before layer phase `phase` (5 per layer) of the first step and
+ * never writes its outputs, so the other CTAs' bounded waits for them expire
+ * (2 s): the kernel records B200_DEVICE_TIMEOUT_GRID, every CTA leaves its
+ * loops and drains its copies, and the context stays usable.  The decode
+ * call's tokens are then undefined; prefill again before decoding.  No GPU
+ * fault is involved. */
+int b200_engine_test_stall(b200_engine_t engine, int phase);
 /* The current decode mode. */
 int b200_engine_decode_mode(b200_engine_t engine);
 /* Device-side error word of the persistent kernel (B200_DEVICE_*; a bounded

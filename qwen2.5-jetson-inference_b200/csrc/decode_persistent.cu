@@ -858,6 +858,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const P
       const bf16* emb = a.embed + size_t(tok) * H;  // x entering layer 0
       const u64* x_in = nullptr;                     // x entering layer l (tagged)
       for (int l = 0; l < a.n_layers; ++l) {
+        if (a.stall_phase >= 0 && blockIdx.x == 0 && step == 0 && phase >= a.stall_phase) {
+          alive = false;  // test hook: the other CTAs' waits for this CTA expire
+          break;
+        }
         const PersistLayer L = a.layers[l];
         u64* w_qkv = a.words + size_t(l) * layer_words;
         u64* w_att = w_qkv + qkv_dim;

@@ -60,6 +60,7 @@ struct b200_engine {
   int mode = B200_ENGINE_DECODE_GRAPH;
   int h_pos = -1;  // position of the next decode step (-1: no prefill yet)
   unsigned long long* trace = nullptr;  // persistent-kernel timeline (optional)
+  int stall_phase = -1;                 // test hook for the next decode call
   int trace_count = 0;
 };
 
@@ -553,6 +554,13 @@ int b200_engine_read_trace(b200_engine_t e, unsigned long long* out) {
   return e->plan.grid;
 }
 
+int b200_engine_test_stall(b200_engine_t e, int phase) {
+  if (e == nullptr) return B200_ERR_INVALID_ARGUMENT;
+  if (e->mode != B200_ENGINE_DECODE_PERSISTENT) return B200_ERR_INVALID_ARGUMENT;
+  e->stall_phase = phase < 0 ? -1 : phase;
+  return B200_OK;
+}
+
 int b200_engine_decode_mode(b200_engine_t e) {
   return e == nullptr ? B200_ERR_INVALID_ARGUMENT : e->mode;
 }
@@ -605,6 +613,8 @@ int b200_engine_decode(b200_engine_t e, int steps) {
     a.status = e->d_status;
     a.trace = e->trace;
     a.trace_count = e->trace_count;
+    a.stall_phase = e->stall_phase;
+    e->stall_phase = -1;
     a.steps = steps;
     e->epoch += unsigned(steps);
     return check(b200::launch_persistent(c.w8 != 0, e->plan, a, e->stream));

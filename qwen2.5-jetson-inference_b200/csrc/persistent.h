@@ -66,6 +66,9 @@ struct PersistArgs {
   // landed, input words arrived] global-timer ns.
   unsigned long long* trace;
   int trace_count;
+  // Test hook (-1: off): CTA 0 stops before layer phase `stall_phase` of the
+  // first step, so every other CTA's bounded wait for its outputs expires.
+  int stall_phase;
   int steps;
   // plan (copied from PersistPlan by launch_persistent)
   int ring_bytes;              // shared memory: weight ring at 0, staging

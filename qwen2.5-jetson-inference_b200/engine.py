@@ -47,6 +47,7 @@ for _name, (_args, _res) in {
     "b200_engine_device_status": ([_p, _i], _i),
     "b200_engine_set_trace": ([_p, _i], _i),
     "b200_engine_force_token": ([_p, _i], _i),
+    "b200_engine_test_stall": ([_p, _i], _i),
     "b200_engine_read_trace": ([_p, _p], _i),
 }.items():
     _fn = getattr(ABI, _name)

@@ -116,3 +116,31 @@ def test_teacher_forced_disagreements_are_near_ties(mods, precision, mode):
         assert gaps[j] <= 0.0625, (j, gaps[j])
     assert e.device_status() == 0
     e.close()
+
+
+def test_persistent_wait_timeout_is_reported_and_recoverable(mods):
+    """Failure path without a GPU fault: CTA 0 withholds its outputs (test
+    hook), the other CTAs' bounded waits expire after ~2 s, the kernel
+    returns with a B200_DEVICE_TIMEOUT_* code in the engine's status word,
+    and the engine decodes correctly afterwards."""
+    import ctypes
+    from qwen25_b200 import ABI
+    e2e, eng = mods
+    prompt = e2e.prompt_ids(16, seed=8)
+    clean = eng.Engine(MODEL_DIR, "w8a16", max_seq=64, mode="persistent")
+    want, _, _ = clean.generate(prompt, 12)
+    clean.close()
+    e = eng.Engine(MODEL_DIR, "w8a16", max_seq=64, mode="persistent")
+    arr = (ctypes.c_int * len(prompt))(*prompt)
+    assert ABI.b200_engine_prefill(e.handle, arr, len(prompt)) == 0
+    assert ABI.b200_engine_test_stall(e.handle, 3) == 0
+    assert ABI.b200_engine_decode(e.handle, 4) == 0
+    # the first wait to expire records its code: a consumer's wait for
+    # CTA 0's words (B200_DEVICE_TIMEOUT_GRID = 3) or a producer's wait for
+    # a ring slot its stalled consumers never free (TIMEOUT_PIPELINE = 1)
+    assert e.device_status(clear=True) in (1, 3)
+    assert e.device_status() == 0
+    got, _, _ = e.generate(prompt, 12)
+    assert got == want
+    assert e.device_status() == 0
+    e.close()
