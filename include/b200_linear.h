@@ -109,7 +109,10 @@ int b200_gemm_w8a16(const int8_t* weight, const uint16_t* scales,
  * bf16(q*s) and the tensor-core BF16 GEMM runs on them (same results as the
  * one-pass kernel).  Without this call the buffer is allocated by the first
  * such GEMM that is not being captured into a CUDA graph; while it is absent
- * the one-pass kernel runs.  Call it before capturing graphs.  No reference
+ * the one-pass kernel runs.  Call it before capturing graphs.  The buffer
+ * is one per device and shared: two such GEMMs running at the same time on
+ * different streams would race on it, so keep large W8A16 GEMMs of a device
+ * in stream order (the reference engine uses one stream).  No reference
  * counterpart (the reference allocates its prefill workspace at start-up,
  * src/qwen2.cpp:80-200). */
 int b200_gemm_reserve_scratch(size_t bytes);
