@@ -72,3 +72,39 @@ def test_quantizer_matches_oracle_bit_exact(b200, oracle):
         qo, so = oracle.quantize_groupwise(w)
         assert np.array_equal(q.numpy(), qo)
         assert np.array_equal(s.view(torch.int16).numpy().view(np.uint16), so)
+
+
+def test_engine_header_symbols_are_exported(b200):
+    text = open(os.path.join(REPO, "include", "b200_engine.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"\b(b200_[a-z0-9_]+)\s*\(", text)))
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(b200.ABI, name), name
+
+
+def test_engine_and_window_reject_bad_arguments_before_the_device(b200):
+    """Null handles and impossible sizes return B200_ERR_INVALID_ARGUMENT (-1)
+    without any CUDA call (so this runs without a GPU)."""
+    import importlib
+    importlib.import_module("qwen25_b200.engine")   # sets the engine argtypes
+    importlib.import_module("qwen25_b200.sharded")  # and the sharded ones
+    A = b200.ABI
+    assert A.b200_engine_decode(None, 1) == -1
+    assert A.b200_engine_prefill(None, None, 4) == -1
+    assert A.b200_engine_set_decode_mode(None, 0) == -1
+    assert A.b200_engine_decode_mode(None) == -1
+    assert A.b200_engine_force_token(None, 5) == -1
+    assert A.b200_engine_test_stall(None, 3) == -1
+    assert A.b200_engine_set_trace(None, 4) == -1
+    assert A.b200_engine_read_trace(None, None) == -1
+    assert A.b200_engine_destroy(None) == 0
+    out = ctypes.c_void_p()
+    assert A.b200_engine_create(ctypes.byref(out), None, None, None, None, None) == -1
+    assert A.b200_window_create(None, 1024, None, ctypes.byref(out)) == -1
+    assert A.b200_window_ptr(None) is None
+    assert A.b200_window_destroy(None) == 0
+    assert A.b200_sharded_gemm_w8a16_p2p(None, None, None, None, 64, None, None,
+                                         4, 8, 16, None) == -1
+    assert A.b200_sharded_gemm_w8a16_p2p(None, None, None, None, 32, None, None,
+                                         4, 8, 16, None) == -2  # group size
