@@ -214,7 +214,10 @@ def per_shape(sweep, calls=200):
 
 
 def gemm_sweep(b200, device, reps=10):
-    """M x five shapes x {W8A16, BF16}; TFLOP/s with CUDA events."""
+    """M x five shapes x {W8A16, BF16}.  `us` / TFLOP/s: device
+    time per call, `reps` calls replayed from a CUDA graph (CUDA events);
+    `us_eager_python`: the same calls launched one by one from Python
+    (ctypes), host launch cost included."""
     gen = torch.Generator(device=device)
     gen.manual_seed(99)
     res = []
@@ -243,9 +246,14 @@ def gemm_sweep(b200, device, reps=10):
                     run()
                 e1.record()
                 torch.cuda.synchronize()
-                t = e0.elapsed_time(e1) / 1e3 / reps
+                t_eager = e0.elapsed_time(e1) / 1e3 / reps
+                # device time: `reps` back-to-back calls replayed from a graph
+                g = capture(lambda: [run() for _ in range(reps)])
+                t = time_graph(g, 3, 1) / reps
+                del g
                 res.append({"w8": w8, "m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
-                            "tflops": round(2.0 * m * n * k / t / 1e12, 1)})
+                            "tflops": round(2.0 * m * n * k / t / 1e12, 1),
+                            "us_eager_python": round(t_eager * 1e6, 2)})
             del x, y
         del q, s, wb
     torch.cuda.empty_cache()

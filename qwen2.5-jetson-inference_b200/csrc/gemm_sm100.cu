@@ -37,6 +37,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -162,7 +163,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_w,
                const bf16* __restrict__ scales, const bf16* __restrict__ bias,
                bf16* __restrict__ out, int m, int n, int k, int ldc,
-               const PeerOuts peers) {
+               const PeerOuts peers, int a_rows) {
   using C = Cfg<kW8, kMSub, kBN>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -228,7 +229,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
             goto producer_done;
           unsigned char* st = stage_base + stage * C::kStageBytes;
           const uint32_t fb = bar_full + 8 * stage;
-          mbar_arrive_expect_tx(fb, C::kTxBytes);
+          // X rows per sub-tile: 128, or fewer for a short prompt (a_rows, the
+          // TMA box height); the MMA's rows beyond them are never stored.
+          mbar_arrive_expect_tx(fb, C::kTxBytes - kMSub * (128 - a_rows) * kBK * 2);
 #pragma unroll
           for (int s = 0; s < kMSub; ++s) {
             tma_load_2d(smem_u32(st + s * C::kABytes), &tmap_x, kb * kBK,
@@ -1023,6 +1026,69 @@ bool make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
   return r == CUDA_SUCCESS;
 }
 
+// Host-side launch costs of a GEMM call, paid once instead of per call: a
+// cache of encoded tensor maps (a map holds only the address, shape, box and
+// swizzle it was encoded with, so equal keys give equal maps), and the
+// dynamic shared-memory attribute set once per kernel and device.
+struct TmapKey {
+  const void* base;
+  int dev, dtype, elem_bytes, inner, outer, box_inner, box_outer, swizzle;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && dev == o.dev && dtype == o.dtype && elem_bytes == o.elem_bytes &&
+           inner == o.inner && outer == o.outer && box_inner == o.box_inner &&
+           box_outer == o.box_outer && swizzle == o.swizzle;
+  }
+};
+struct TmapEntry {
+  TmapKey key;
+  CUtensorMap map;
+  bool valid = false;
+};
+constexpr int kTmapCacheSize = 128;
+std::mutex g_tmap_mutex;
+TmapEntry g_tmap_cache[kTmapCacheSize];
+unsigned g_tmap_next = 0;
+
+bool make_tmap_cached(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                      int elem_bytes, int inner, int outer, int box_inner, int box_outer,
+                      CUtensorMapSwizzle swizzle) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const TmapKey key{base, dev, int(dtype), elem_bytes, inner, outer, box_inner, box_outer,
+                    int(swizzle)};
+  {
+    std::lock_guard<std::mutex> lock(g_tmap_mutex);
+    for (const TmapEntry& e : g_tmap_cache) {
+      if (e.valid && e.key == key) {
+        *map = e.map;
+        return true;
+      }
+    }
+  }
+  if (!make_tmap(map, base, dtype, elem_bytes, inner, outer, box_inner, box_outer, swizzle)) {
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(g_tmap_mutex);
+  TmapEntry& slot = g_tmap_cache[g_tmap_next++ % kTmapCacheSize];
+  slot.key = key;
+  slot.map = *map;
+  slot.valid = true;
+  return true;
+}
+
+template <auto kKernel>
+cudaError_t ensure_smem_attr(int bytes) {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
+
 int sm_count() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1037,26 +1103,27 @@ cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
                        int ldc, const PeerOuts& peers, cudaStream_t stream) {
   using C = Cfg<kW8, kMSub, kBN>;
   CUtensorMap tx, tw;
-  if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
+  // A short prompt (m < 128, one 128-row sub-tile) loads only its rows.
+  const int a_rows = (kMSub == 1 && m < 128) ? (m + 7) / 8 * 8 : 128;
+  if (!make_tmap_cached(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, a_rows,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if (kW8) {
-    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, kBN,
+    if (!make_tmap_cached(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, kBN,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
   } else {
-    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK,
+    if (!make_tmap_cached(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK,
                    kBN, CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
   auto kernel = gemm_tc_kernel<kW8, kMSub, kBN>;
-  cudaError_t e = cudaFuncSetAttribute(
-      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  cudaError_t e = ensure_smem_attr<gemm_tc_kernel<kW8, kMSub, kBN>>(C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int tiles = ((m + C::kBM - 1) / C::kBM) * ((n + kBN - 1) / kBN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, scales, bias,
-                                                        output, m, n, k, ldc, peers);
+                                                        output, m, n, k, ldc, peers, a_rows);
   return cudaGetLastError();
 }
 
@@ -1066,21 +1133,20 @@ cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias
                         int ldc, const PeerOuts& peers, cudaStream_t stream) {
   using C = Cfg2<kW8>;
   CUtensorMap tx, tw;
-  if (!make_tmap(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
+  if (!make_tmap_cached(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if (kW8) {
-    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, C::kHalf,
+    if (!make_tmap_cached(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, C::kHalf,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
   } else {
-    if (!make_tmap(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK, C::kHalf,
+    if (!make_tmap_cached(&tw, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK, C::kHalf,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
   auto kernel = gemm_tc2_kernel<kW8>;
-  cudaError_t e = cudaFuncSetAttribute(
-      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  cudaError_t e = ensure_smem_attr<gemm_tc2_kernel<kW8>>(C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int tiles = ((m + 255) / 256) * ((n + C::kBN - 1) / C::kBN);
   const int pairs = sm_count() / 2;
@@ -1107,7 +1173,7 @@ bool aligned16(const void* p) {
 
 // Tile-shape choice: the largest tile that still gives every SM work.
 // B200_GEMM_TILE=pair|256x128|128x256|128x128|128x64 overrides it (tuning only).
-enum class Tile { kPair256x256, k256x128, k128x256, k128x128, k128x64 };
+enum class Tile { kPair256x256, k256x128, k128x256, k128x128, k128x64, k128x32 };
 
 // BF16 prefers the CTA-pair 256x256 tile, then 128x256 (one N=256 MMA per
 // k-step reads less shared memory per FLOP than two M=128 x N=128 MMAs);
@@ -1122,6 +1188,7 @@ Tile choose_tile(bool w8, int m, int n) {
     if (!strcmp(forced, "128x256")) return Tile::k128x256;
     if (!strcmp(forced, "128x128")) return Tile::k128x128;
     if (!strcmp(forced, "128x64")) return Tile::k128x64;
+    if (!strcmp(forced, "128x32") && !w8) return Tile::k128x32;
   }
   const long long sms = sm_count();
   const long long t256x128 = ((m + 255) / 256) * (long long)((n + 127) / 128);
@@ -1132,6 +1199,11 @@ Tile choose_tile(bool w8, int m, int n) {
   if (!w8 && t128x256 >= sms) return Tile::k128x256;
   if (t256x128 >= sms) return Tile::k256x128;
   if (t128x128 >= sms / 2) return Tile::k128x128;
+  // Few tokens and few columns: each tile walks all of K, so the GEMM takes
+  // as long as one tile's K walk; narrower BF16 tiles put more SMs on it
+  // (same per-element K order, so the same results).
+  const long long t128x64 = ((m + 127) / 128) * (long long)((n + 63) / 64);
+  if (!w8 && t128x64 < sms / 4) return Tile::k128x32;
   return Tile::k128x64;
 }
 
@@ -1152,6 +1224,12 @@ cudaError_t launch_tile(Tile t, const void* weight, const bf16* scales,
     case Tile::k128x128:
       return launch_cfg<kW8, 1, 128>(weight, scales, bias, input, output, m, n, k, ldc, peers,
                                      stream);
+    case Tile::k128x32:
+      if constexpr (!kW8) {
+        return launch_cfg<false, 1, 32>(weight, scales, bias, input, output, m, n, k, ldc, peers,
+                                        stream);
+      }
+      [[fallthrough]];
     default:
       return launch_cfg<kW8, 1, 64>(weight, scales, bias, input, output, m, n, k, ldc, peers,
                                     stream);
@@ -1185,6 +1263,12 @@ namespace {
 
 constexpr size_t kScratchCap = size_t(256) << 20;
 constexpr int kTwoPassMinTokens = 1024;
+// Few tokens with a long K (a short prompt through down_proj): the one-pass
+// kernel's per-k-block dequant hand-off makes each tile's K walk slow and
+// there are few tiles; dequantising W once and running narrow BF16 tiles
+// is faster, with the same results.
+constexpr int kTwoPassMaxFewTokens = 128;
+constexpr int kTwoPassFewTokensMinK = 2048;
 
 struct Scratch {
   void* ptr = nullptr;
@@ -1290,7 +1374,9 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
-  if (w8 && m >= kTwoPassMinTokens && !getenv("B200_GEMM_ONE_PASS")) {
+  if (w8 && (m >= kTwoPassMinTokens ||
+             (m <= kTwoPassMaxFewTokens && k >= kTwoPassFewTokensMinK)) &&
+      !getenv("B200_GEMM_ONE_PASS")) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(stream, &cap);
     Scratch sc;
