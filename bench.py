@@ -260,25 +260,60 @@ def gemm_sweep(b200, device, reps=10):
     return res
 
 
+def sharded_shard(b200, j, q_rank, nr, k, device):
+    """Shard q_rank's W8A16 weights of sharded case j (seeded per case and
+    shard, so any rank can rebuild any shard for the check)."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(100 + 16 * j + q_rank)
+    w = torch.randn(nr, k, generator=gen, device=device) * 0.02
+    return b200.quantize_groupwise(w)
+
+
+def sharded_check(b200, sh, j, world, m, k, n, x, outputs, device):
+    """Checks sampled rows x sampled columns of every shard of the gathered
+    outputs against a torch FP32 product of X with bf16(q*s) (the GEMM's
+    arithmetic), within the tolerance |d| <= 2e-2 + 1e-2 |ref|.  Returns
+    (ok, max abs error)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device="cpu")
+    g.manual_seed(4242 + j)
+    rows = torch.randint(0, m, (6,), generator=g).tolist() + [0, m - 1]
+    ok, worst = True, 0.0
+    xr = x[rows].float()
+    for q_rank in range(world):
+        r0, nr = sh.shard_range(n, world, q_rank)
+        q, s = sharded_shard(b200, j, q_rank, nr, k, device)
+        cols = torch.randint(0, nr, (24,), generator=g).tolist() + [0, nr - 1]
+        deq = (q[cols].float() * s[cols].float().repeat_interleave(64, dim=1)[:, :k])
+        deq = deq.to(torch.bfloat16).float()
+        ref = xr @ deq.t()
+        for y in outputs:
+            got = y[rows][:, [r0 + c for c in cols]].float()
+            err = (got - ref).abs()
+            worst = max(worst, float(err.max()))
+            ok = ok and bool((err <= 2e-2 + 1e-2 * ref.abs()).all())
+        del q, s
+    return ok, worst
+
+
 def sharded_bench(b200, world, rank, device, reps=5):
     """column-sharded W8A16 GEMM (M=8192; K,N = 8192,28672 and
     28672,8192) with the NCCL all-gather and in its fused form (epilogue
     stores into every rank's window over NVLink), and the vocabulary-sharded LM head
     (896 -> 151936, M=1) with the cross-GPU argmax.  Device time, max over
-    ranks; TFLOP/s counts the whole (unsharded) GEMM."""
+    ranks; TFLOP/s counts the whole (unsharded) GEMM.  After timing, the
+    gathered outputs of both forms are checked on sampled rows and columns of
+    every shard, and the LM head's argmax against the unsharded kernel."""
     import importlib
     sh = importlib.import_module("qwen25_b200.sharded")
     comm = (sh.Comm.from_process_group() if world > 1
             else sh.Comm(sh.new_unique_id(), 1, 0))
-    gen = torch.Generator(device=device)
-    gen.manual_seed(100 + rank)
     out = {"gemm": [], "lm_head": None}
+    checks = []
     m = 8192
-    for (k, n) in [(8192, 28672), (28672, 8192)]:
+    for j, (k, n) in enumerate([(8192, 28672), (28672, 8192)]):
         r0, nr = sh.shard_range(n, world, rank)
-        w = torch.randn(nr, k, generator=gen, device=device) * 0.02
-        q, s = b200.quantize_groupwise(w)
-        del w
+        q, s = sharded_shard(b200, j, rank, nr, k, device)
         xg = torch.Generator(device=device)
         xg.manual_seed(7)  # X replicated: same seed on every rank
         x = torch.randn(m, k, generator=xg, device=device).to(torch.bfloat16)
@@ -313,14 +348,48 @@ def sharded_bench(b200, world, rank, device, reps=5):
             res[name + "_ms"] = round(t * 1e3, 3)
         res["tflops"] = round(2.0 * m * n * k / (res["sharded_ms"] / 1e3) / 1e12, 1)
         res["tflops_fused_p2p"] = round(2.0 * m * n * k / (res["fused_p2p_ms"] / 1e3) / 1e12, 1)
+        del ws, yl
+        torch.cuda.empty_cache()
+        if world > 1:
+            # the same whole GEMM on one GPU, timed in this run (every rank
+            # runs it on its own GPU; max over ranks)
+            qf, sf = b200.quantize_groupwise(torch.randn(n, k, device=device) * 0.02)
+            yf = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+            for _ in range(2):
+                b200.gemm_w8a16(qf, sf, 64, None, x, yf, m, n, k)
+            torch.cuda.synchronize()
+            barrier(world)
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            for _ in range(reps):
+                b200.gemm_w8a16(qf, sf, 64, None, x, yf, m, n, k)
+            e1.record()
+            torch.cuda.synchronize()
+            t1 = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
+            res["one_gpu_ms"] = round(t1 * 1e3, 3)
+            res["eff_vs_1gpu_fused_p2p"] = round(t1 / (world * res["fused_p2p_ms"] / 1e3), 3)
+            del qf, sf, yf
+            torch.cuda.empty_cache()
+        full()
+        fused()
+        torch.cuda.synchronize()
+        ok, worst = sharded_check(b200, sh, j, world, m, k, n, x,
+                                  [y, win.tensor((m, n))], device)
+        ok = max_over_ranks(0.0 if ok else 1.0, world) == 0.0
+        res["check"] = "pass" if ok else "fail"
+        res["check_max_abs_err"] = round(max_over_ranks(worst, world), 5)
+        checks.append(ok)
         out["gemm"].append(res)
         win.close()
-        del q, s, x, y, ws, yl
+        del q, s, x, y
         torch.cuda.empty_cache()
     v, k = 151936, 896
     v0, vn = sh.shard_range(v, world, rank)
-    wl = (torch.randn(vn, k, generator=gen, device=device) * 0.02).to(torch.bfloat16)
-    xl = torch.randn(k, generator=gen, device=device).to(torch.bfloat16)
+    gl = torch.Generator(device=device)
+    gl.manual_seed(900)  # the full LM-head matrix, same on every rank
+    wfull = (torch.randn(v, k, generator=gl, device=device) * 0.02).to(torch.bfloat16)
+    xl = torch.randn(k, generator=gl, device=device).to(torch.bfloat16)
+    wl = wfull[v0:v0 + vn].contiguous()
     logits = torch.empty(vn, dtype=torch.bfloat16, device=device)
     wsl = sh.lm_head_workspace(v, world, device)
     am = torch.empty(1, dtype=torch.int32, device=device)
@@ -335,8 +404,21 @@ def sharded_bench(b200, world, rank, device, reps=5):
     e1.record()
     torch.cuda.synchronize()
     t = max_over_ranks(e0.elapsed_time(e1) / 1e3 / 20, world)
+    # check: the sharded argmax equals the unsharded fused LM head's
+    full_logits = torch.empty(v, dtype=torch.bfloat16, device=device)
+    bv, bi = b200.lm_head_workspace(v, device)
+    am1 = torch.empty(1, dtype=torch.int32, device=device)
+    b200.lm_head_bf16(wfull, None, xl, full_logits, bv, bi, am1, v, k)
+    torch.cuda.synchronize()
+    ok = int(am.item()) == int(am1.item()) and torch.equal(logits, full_logits[v0:v0 + vn])
+    ok = max_over_ranks(0.0 if ok else 1.0, world) == 0.0
+    checks.append(ok)
     out["lm_head"] = {"vocab": v, "k": k, "us": round(t * 1e6, 2),
-                      "gbs_per_gpu": round(2 * (v // world) * k / t / 1e9, 1)}
+                      "gbs_per_gpu": round(2 * (v // world) * k / t / 1e9, 1),
+                      "check": "pass" if ok else "fail"}
+    out["check"] = "pass" if all(checks) else "fail"
+    del wfull
+    torch.cuda.empty_cache()
     comm.close()
     return out
 
@@ -422,7 +504,7 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
 
 
 # ------------------------------------------------------------ CPU reference
-def cpu_reference_sample(steps, warmup, budget_s=12.0):
+def cpu_reference_sample(steps, warmup, budget_s=12.0, min_s=0.0):
     """Reference src/cpu_ops.cpp linear_fp32 (OpenBLAS sgemv, FP32 weights) on
     the same five shapes; value in the same metric (W8A16 algorithmic bytes
     of the sweep / time).  Returns (value_gbs, cores, sample text)."""
@@ -457,7 +539,8 @@ def cpu_reference_sample(steps, warmup, budget_s=12.0):
             fn(w, b, x)
             total += nb
         passes += 1
-        if passes >= steps or time.perf_counter() - t0 > budget_s:
+        el = time.perf_counter() - t0
+        if (passes >= steps and el >= min_s) or el > budget_s:
             break
     dt = time.perf_counter() - t0
     return total / dt / 1e9, cores, kind, (
@@ -512,7 +595,9 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    value, cores, kind, sample = cpu_reference_sample(args.steps, args.warmup)
+    # at least `steps` passes and at least 6 s of CPU work (20 s at most)
+    value, cores, kind, sample = cpu_reference_sample(args.steps, args.warmup,
+                                                      budget_s=20.0, min_s=6.0)
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -714,6 +799,9 @@ def main():
                 traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                 "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                  "launch, read from profiles/gemv_w8a16_896x151936.md "
+                                  "(not measured in this run)",
                 "peak_kind": peak_kind, "kernel": "gemv_bulk_kernel<W8> 896->151936",
                 "algorithmic_bytes_per_launch": big["bytes"],
                 "us_per_launch": round(t_big * 1e6, 2)}

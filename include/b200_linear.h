@@ -187,8 +187,11 @@ int b200_window_destroy(b200_window_t window);
 /* The fused form of b200_sharded_gemm_w8a16_allgather: the local
  * tensor-core GEMM stores each output tile straight into the window of
  * every rank (16-byte stores over NVLink from its epilogue, so the exchange
- * overlaps the math tile by tile), then a 4-byte NCCL all-reduce on `stream`
- * orders every rank's stores before what follows on any rank's stream.  On
+ * overlaps the math tile by tile).  Two 4-byte NCCL all-reduces on `stream`
+ * order it: one before the GEMM (no rank writes into a window that another
+ * rank's stream may still be reading from the previous call, so one window
+ * can serve call after call) and one after it (every rank's stores land
+ * before what follows on any rank's stream).  On
  * completion the window holds the full row-major Y[tokens, out_features] on
  * every rank; the window must hold at least tokens x out_features BF16.
  * No gather workspace and no layout copy.  Same arguments and limits

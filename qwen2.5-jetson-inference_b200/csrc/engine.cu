@@ -583,7 +583,8 @@ int b200_engine_decode(b200_engine_t e, int steps) {
   // decoded tokens must fit max_seq.
   if (e->h_pos < 0) return B200_ERR_INVALID_ARGUMENT;
   if (steps > e->cfg.max_seq - e->h_pos) return B200_ERR_TOO_LARGE;
-  e->h_pos += steps;
+  // h_pos mirrors the device position: it advances only by the steps whose
+  // launches were accepted, so a failed launch leaves it consistent.
   if (e->mode == B200_ENGINE_DECODE_PERSISTENT) {
     const auto& c = e->cfg;
     b200::PersistArgs a = {};
@@ -616,8 +617,11 @@ int b200_engine_decode(b200_engine_t e, int steps) {
     a.stall_phase = e->stall_phase;
     e->stall_phase = -1;
     a.steps = steps;
+    const int rc = check(b200::launch_persistent(c.w8 != 0, e->plan, a, e->stream));
+    if (rc != B200_OK) return rc;
     e->epoch += unsigned(steps);
-    return check(b200::launch_persistent(c.w8 != 0, e->plan, a, e->stream));
+    e->h_pos += steps;
+    return B200_OK;
   }
   if (e->graph == nullptr) {
     cudaGraph_t g = nullptr;
@@ -630,7 +634,10 @@ int b200_engine_decode(b200_engine_t e, int steps) {
     cudaGraphDestroy(g);
     ENGINE_TRY(check(inst));
   }
-  for (int i = 0; i < steps; ++i) ENGINE_TRY(check(cudaGraphLaunch(e->graph, e->stream)));
+  for (int i = 0; i < steps; ++i) {
+    ENGINE_TRY(check(cudaGraphLaunch(e->graph, e->stream)));
+    e->h_pos += 1;
+  }
   return B200_OK;
 }
 

@@ -866,6 +866,56 @@ bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
          aligned16(weight) && aligned16(input);
 }
 
+namespace {
+
+// Which kernel a call runs and with what geometry; computed before any
+// launch so that callers with a fixed-size partials buffer can check the
+// grid first (b200_lm_head_bf16_noalloc).
+struct GemvPlan {
+  int kind = 0;  // 0: nothing to do, 1: generic, 2: TMA bulk, 3: stream
+  BulkPlan bulk;
+  GemvConfig cfg{0, 0};
+  int grid = 0;
+};
+
+int stream_rows_per_block(int tpr, int r) { return (kThreads / tpr) * r; }
+
+GemvPlan plan_gemv(bool w8, const void* weight, const bf16* scales, int n,
+                   int k, const void* input, bool lm_head) {
+  GemvPlan plan;
+  if (n <= 0) return plan;
+  if (!gemv_uses_fast_path(w8, weight, input, k)) {
+    plan.kind = 1;
+    plan.grid = (n + 7) / 8;
+    return plan;
+  }
+  // TMA-bulk path: needs whole 8-row tiles of 16-byte multiples (n % 8) and
+  // 16-byte aligned scales.
+  if (n % 8 == 0 && (!w8 || aligned16(scales))) {
+    // The LM-head form writes one argmax partial per CTA into a workspace of
+    // ceil(n / 8) entries: tiles of >= 8 rows keep the grid within it.
+    plan.bulk = plan_bulk(w8, n, k, lm_head ? 8 : 1);
+    if (plan.bulk.lpr > 0) {
+      plan.kind = 2;
+      plan.grid = plan.bulk.grid;
+      return plan;
+    }
+  }
+  const int chunks = w8 ? k / 16 : k / 8;
+  plan.kind = 3;
+  plan.cfg = choose_config(n, chunks, lm_head);
+  const int rows = stream_rows_per_block(plan.cfg.tpr, plan.cfg.r);
+  plan.grid = (n + rows - 1) / rows;
+  return plan;
+}
+
+}  // namespace
+
+int gemv_grid(bool w8, const void* weight, const bf16* scales,
+              const void* input, int n, int k, bool lm_head) {
+  return plan_gemv(w8, weight, scales, n, k, input, lm_head).grid;
+}
+
 cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
                         const bf16* bias, const bf16* input, bf16* output,
                         int n, int k, float* block_value, int* block_index,
@@ -875,51 +925,41 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
   const GemvFusion& f = fusion ? *fusion : nofusion;
   const bool fused = fusion != nullptr &&
                      (f.in_mode != 0 || f.residual != nullptr);
-  if (n <= 0) {
-    if (grid_out) *grid_out = 0;
-    return cudaSuccess;
-  }
-  if (!gemv_uses_fast_path(w8, weight, input, k)) {
-    if (fused) return cudaErrorNotSupported;
+  const GemvPlan plan =
+      plan_gemv(w8, weight, scales, n, k, input, block_value != nullptr);
+  if (grid_out) *grid_out = plan.grid;
+  if (plan.kind == 0) return cudaSuccess;
+  // The fusions exist only in the TMA-bulk kernel.
+  if (fused && plan.kind != 2) return cudaErrorNotSupported;
+  if (plan.kind == 1) {
     return w8 ? launch_generic<true>(weight, scales, bias, input, output, n, k,
-                                     block_value, block_index, stream, grid_out)
+                                     block_value, block_index, stream, nullptr)
               : launch_generic<false>(weight, scales, bias, input, output, n,
                                       k, block_value, block_index, stream,
-                                      grid_out);
+                                      nullptr);
   }
-  // TMA-bulk path: needs whole 8-row tiles of 16-byte multiples (n % 8) and
-  // 16-byte aligned scales.
-  const bool bulk_ok = n % 8 == 0 && (!w8 || aligned16(scales));
-  if (bulk_ok) {
-    // The LM-head form writes one argmax partial per CTA into a workspace of
-    // ceil(n / 8) entries: tiles of >= 8 rows keep the grid within it.
-    const BulkPlan p = plan_bulk(w8, n, k, block_value != nullptr ? 8 : 1);
-    if (p.lpr > 0) {
-      if (grid_out) *grid_out = p.grid;
-      return w8 ? dispatch_bulk<true>(p, weight, scales, bias, input, output, n,
-                                      k, block_value, block_index, stream, f)
-                : dispatch_bulk<false>(p, weight, scales, bias, input, output,
-                                       n, k, block_value, block_index, stream, f);
-    }
+  if (plan.kind == 2) {
+    const BulkPlan& p = plan.bulk;
+    return w8 ? dispatch_bulk<true>(p, weight, scales, bias, input, output, n,
+                                    k, block_value, block_index, stream, f)
+              : dispatch_bulk<false>(p, weight, scales, bias, input, output,
+                                     n, k, block_value, block_index, stream, f);
   }
-  // The fusions exist only in the TMA-bulk kernel.
-  if (fused) return cudaErrorNotSupported;
-  const int chunks = w8 ? k / 16 : k / 8;
-  const GemvConfig c = choose_config(n, chunks, block_value != nullptr);
+  const GemvConfig c = plan.cfg;
   if (w8) {
     return c.r == 4 ? dispatch_tpr<true, 4>(c.tpr, weight, scales, bias, input,
                                             output, n, k, block_value,
-                                            block_index, stream, grid_out)
+                                            block_index, stream, nullptr)
                     : dispatch_tpr<true, 1>(c.tpr, weight, scales, bias, input,
                                             output, n, k, block_value,
-                                            block_index, stream, grid_out);
+                                            block_index, stream, nullptr);
   }
   return c.r == 4 ? dispatch_tpr<false, 4>(c.tpr, weight, scales, bias, input,
                                            output, n, k, block_value,
-                                           block_index, stream, grid_out)
+                                           block_index, stream, nullptr)
                   : dispatch_tpr<false, 1>(c.tpr, weight, scales, bias, input,
                                            output, n, k, block_value,
-                                           block_index, stream, grid_out);
+                                           block_index, stream, nullptr);
 }
 
 cudaError_t read_gemv_status(int* value, bool clear) {

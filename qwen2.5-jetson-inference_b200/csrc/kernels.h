@@ -26,6 +26,10 @@ struct GemvFusion {
 // gemv.cu
 bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
                          int k);
+// CTA count launch_gemv will use for these arguments (lm_head: the form with
+// argmax partials), without launching anything; 0 when n <= 0.
+int gemv_grid(bool w8, const void* weight, const bf16* scales,
+              const void* input, int n, int k, bool lm_head);
 // Launches the GEMV (block_value == nullptr) or the LM-head GEMV with
 // per-CTA argmax partials; *grid_out receives the CTA count.
 cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,

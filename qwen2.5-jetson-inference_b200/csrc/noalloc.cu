@@ -82,13 +82,16 @@ int b200_lm_head_bf16_noalloc(const uint16_t* weight, const uint16_t* bias,
   const auto* b = reinterpret_cast<const b200::bf16*>(bias);
   const auto* x = reinterpret_cast<const b200::bf16*>(input);
   auto* y = reinterpret_cast<b200::bf16*>(logits);
+  // The partials array holds kMaxPartials entries: check the launch's CTA
+  // count before anything is enqueued (every launch shape has >= 8 rows per
+  // CTA, so the vocab limit above already keeps it within range).
+  const int planned = b200::gemv_grid(false, w, nullptr, x, vocab, in_features,
+                                      /*lm_head=*/true);
+  if (planned > kMaxPartials) return B200_ERR_TOO_LARGE;
   int grid = 0;
   e = b200::launch_gemv(false, w, nullptr, b, x, y, vocab, in_features,
                         block_value, block_index, stream, &grid);
   if (e != cudaSuccess) return int(e);
-  // Cannot trigger: every launch shape has >= 8 rows per CTA and vocab is
-  // limited to 8 * kMaxPartials above.
-  if (grid > kMaxPartials) return B200_ERR_TOO_LARGE;
   e = b200::launch_argmax_partials(block_value, block_index, grid, argmax,
                                    stream);
   return e == cudaSuccess ? B200_OK : int(e);

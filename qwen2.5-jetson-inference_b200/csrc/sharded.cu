@@ -54,6 +54,9 @@ struct b200_window {
 };
 
 namespace b200 {
+
+constexpr int kMaxRanks = 8;  // ranks of one node (windows map at most 8)
+
 namespace {
 
 // [P][M][Ns] -> [M][P*Ns], 16 bytes per thread per step.
@@ -190,23 +193,29 @@ exchange_argmax_kernel(const float* __restrict__ block_value,
       const unsigned int gi = unsigned(bi + index_offset);
       k = (static_cast<unsigned long long>(float_order_key(b)) << 32) | (0xFFFFFFFFull - gi);
     }
-    // slot layout per window: [rank][key, seq]
+    // Slot layout per window: [seq parity][rank][key, seq].  Consecutive
+    // calls use different halves, so a rank that is one call ahead never
+    // overwrites a key that a slower rank has not read yet; it cannot get two
+    // calls ahead, since finishing call seq+1 needs the slower rank's key of
+    // call seq+1, published only after that rank has read call seq.
+    const int half = int(seq & 1ull) * 2 * kMaxRanks;
     for (int q = 0; q < nranks; ++q) {
-      volatile unsigned long long* dst = windows.slot[q] + 2 * rank;
+      volatile unsigned long long* dst = windows.slot[q] + half + 2 * rank;
       dst[0] = k;
     }
     __threadfence_system();
     for (int q = 0; q < nranks; ++q) {
-      volatile unsigned long long* dst = windows.slot[q] + 2 * rank;
+      volatile unsigned long long* dst = windows.slot[q] + half + 2 * rank;
       dst[1] = seq;
     }
   }
   if (threadIdx.x < nranks) {
-    volatile unsigned long long* mine = windows.slot[rank] + 2 * threadIdx.x;
+    const int half = int(seq & 1ull) * 2 * kMaxRanks;
+    volatile unsigned long long* mine = windows.slot[rank] + half + 2 * threadIdx.x;
     const uint64_t start = global_timer_ns();
     unsigned long long k = 0ull;
     while (true) {
-      if (mine[1] == seq) {
+      if (mine[1] >= seq) {
         __threadfence_system();
         k = mine[0];
         break;
@@ -421,6 +430,14 @@ int b200_sharded_gemm_w8a16_p2p(b200_comm_t comm, b200_window_t out,
     peers.delta[peers.n++] =
         static_cast<char*>(out->peer[r]) - static_cast<char*>(out->local);
   }
+  if (p > 1) {
+    // Entry ordering point: no rank stores into a peer's window before every
+    // rank has finished what its stream enqueued earlier, including reads of
+    // the window's previous contents (the window is reused call after call).
+    const int rc = b200::nccl_status(
+        ncclAllReduce(out->token, out->token, 1, ncclInt32, ncclSum, comm->nccl, s));
+    if (rc != B200_OK) return rc;
+  }
   cudaError_t e = b200::launch_gemm_tc_peers(
       true, weight_shard, reinterpret_cast<const bf16*>(scales_shard),
       reinterpret_cast<const bf16*>(bias_shard), reinterpret_cast<const bf16*>(input), mine,
@@ -520,7 +537,7 @@ int b200_sharded_lm_head_bf16(b200_comm_t comm, const uint16_t* weight_shard,
     // Cross-GPU argmax through the key window (created on the first call,
     // collectively: every rank makes the same sequence of calls).
     if (comm->keys == nullptr) {
-      const int rc = b200_window_create(comm, 2 * 8 * sizeof(unsigned long long), stream,
+      const int rc = b200_window_create(comm, 2 * 2 * b200::kMaxRanks * sizeof(unsigned long long), stream,
                                         &comm->keys);
       if (rc != B200_OK) return rc;
     }

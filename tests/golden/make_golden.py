@@ -1,7 +1,7 @@
 """Generates the CPU golden fixtures in this directory from the REFERENCE itself.
 
-Run in a container that has the reference checkout (default /root/reference,
-override with --reference) and the reference CPU Linear built into
+Run in a container that has the reference checkout (--reference, default
+$QWEN_REFERENCE_DIR or BASELINE.json's reference_path) and the reference CPU Linear built into
 oracle/_ref (``make -C oracle ref``):
 
     python tests/golden/make_golden.py
@@ -50,8 +50,13 @@ BF16_CASES = [(3, 11, 14, True), (2, 5, 7, True), (3, 23, 14, False),
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     args = ap.parse_args()
+    if args.reference is None:
+        args.reference = os.environ.get("QWEN_REFERENCE_DIR")
+    if args.reference is None:
+        with open(os.path.join(REPO, "BASELINE.json")) as f:
+            args.reference = json.load(f)["reference_path"]
     sys.path.insert(0, os.path.join(args.reference, "tools"))
     import export_model as E  # the reference exporter
     from oracle import oracle as O

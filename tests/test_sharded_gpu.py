@@ -90,17 +90,31 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _run_worker(nproc, shapes):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1",
+           f"--master-port={_free_port()}",
+           os.path.join(REPO, "tests", "sharded_worker.py"), "--shapes", shapes]
+    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    assert proc.stdout.count(" ok") == nproc, proc.stdout[-3000:]
+    return proc.stdout
+
+
+def test_sharded_full_shapes_one_rank(b200, cuda):
+    """configs[4] shapes (M=8192, 8192->28672 and 28672->8192; the 151936
+    LM head) on a one-rank communicator, checked against the oracle."""
+    _run_worker(1, "full")
+
+
 def test_multi_gpu_sharded_linear(b200, cuda):
+    """Every visible GPU (2..8): small shapes, then the configs[4] shapes,
+    gathered outputs and the cross-GPU argmax checked against the oracle."""
     import torch
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 or more GPUs")
     n = min(n, 8)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={n}", "--master-addr=127.0.0.1",
-           f"--master-port={_free_port()}",
-           os.path.join(REPO, "tests", "sharded_worker.py")]
-    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
-    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
-    assert proc.stdout.count(" ok") == n
+    _run_worker(n, "small")
+    _run_worker(n, "full")
