@@ -64,6 +64,29 @@ const char* b200_status_string(int status);
  * current device. */
 int b200_device_status(int clear);
 
+/* Summation order of the decode GEMVs and the fused LM heads.
+ *   B200_ORDER_FAST (default): the fastest order per shape (FP32 throughout;
+ *     outputs within one BF16 ulp of the reference, almost always equal).
+ *   B200_ORDER_REFERENCE: every FP32 operation in the reference kernels'
+ *     order, flushing denormals as the reference build does (--use_fast_math):
+ *     one warp per row (four per row when a GEMV has in_features > 1024),
+ *     16-element INT8 / 8-element BF16 chunks strided over the lanes, each
+ *     chunk a fresh FMA chain, lane sums in chunk order, the __shfl_down tree,
+ *     split-row partials in warp order (reference src/cuda/kernels.cu:359-384,
+ *     438-490, 492-568, 953-1041).  Bit-identical outputs to the reference
+ *     kernels on their fast paths (16-byte aligned weight and input,
+ *     in_features % 8 == 0 for BF16, % 64 == 0 for W8A16) when out_features
+ *     % 8 == 0; other shapes keep the fast order.  The prefill GEMMs need no
+ *     mode: their tensor-core K order already gives the reference's results.
+ * Process-wide; the initial value comes from the environment variable
+ * B200_SUMMATION_ORDER ("reference" or "fast").  Affects launches made
+ * after the call.  No reference counterpart (a numerics switch of this
+ * library). */
+#define B200_ORDER_FAST 0
+#define B200_ORDER_REFERENCE 1
+int b200_set_summation_order(int order);
+int b200_summation_order(void);
+
 /* Decode GEMV, BF16 weights: output[n] = bf16(sum_k W[n,k] x[k] + b[n]).
  * Replaces infer::cuda::gemv_bf16 (reference include/infer/cuda_ops.hpp:24-26,
  * src/cuda/kernels.cu:1540-1564).  Any out_features/in_features >= 0 and any

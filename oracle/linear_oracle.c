@@ -178,3 +178,75 @@ void oracle_quantize_groupwise(const float* weight, int rows, int columns,
     }
   }
 }
+
+/* Decode GEMV / LM-head logits in the reference CUDA kernels' exact FP32
+ * operation order (bit-exact restatement of their arithmetic; denormals are
+ * not flushed here, which the reference's --use_fast_math build does; no
+ * realistic Linear produces them).  Returns BF16 bits in `out`.
+ *   w8 = 1: gemv_w8a16_fast_kernel (src/cuda/kernels.cu:953-1041, 1627-1655):
+ *     16-element chunks; chunk dot d = fma(q0*s, x0, 0), d = fma(q_i*s, x_i, d).
+ *   w8 = 0: gemv_bf16_fast_kernel / lm_head_bf16_kernel (kernels.cu:359-384,
+ *     438-490, 492-568): 8-element chunks (dot_bf16_eight:
+ *     d = fma(w0, x0, w1*x1); d = fma(w2j, x2j, fma(w2j+1, x2j+1, d))).
+ *   Lane l of warp slice ws (of W warps per row) adds chunks
+ *   l + 32*ws + 32*W*j to a sum starting at 0; the 32 lane sums meet in the
+ *   __shfl_down tree (lane i += lane i+off, off = 16..1); W > 1 partials are
+ *   added in warp order to 0; then + bias, BF16 RNE.
+ *   W = 4 when in_features > 1024 for a GEMV (kernels.cu:1547-1558,
+ *   1636-1651), W = 1 otherwise and always for the BF16 LM head. */
+void oracle_gemv_reference_order(const void* weight, int w8, const uint16_t* scales,
+                                 const uint16_t* bias, const uint16_t* input,
+                                 uint16_t* out, int n_rows, int k, int lm_head) {
+  const int epc = w8 ? 16 : 8;
+  const int chunks = k / epc;
+  const int groups = k / 64;
+  const int wpr = (k > 1024 && (w8 || !lm_head)) ? 4 : 1;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < n_rows; ++r) {
+    float partial[4];
+    for (int ws = 0; ws < wpr; ++ws) {
+      float lane_sum[32];
+      for (int l = 0; l < 32; ++l) {
+        float sum = 0.0f;
+        for (int c = l + 32 * ws; c < chunks; c += 32 * wpr) {
+          float d;
+          if (w8) {
+            const int8_t* q = (const int8_t*)weight + (int64_t)r * k + c * 16;
+            const float s = oracle_bf16_to_f32(scales[(int64_t)r * groups + c / 4]);
+            const uint16_t* x = input + c * 16;
+            d = fmaf((float)q[0] * s, oracle_bf16_to_f32(x[0]), 0.0f);
+            for (int e = 1; e < 16; ++e) {
+              d = fmaf((float)q[e] * s, oracle_bf16_to_f32(x[e]), d);
+            }
+          } else {
+            const uint16_t* w = (const uint16_t*)weight + (int64_t)r * k + c * 8;
+            const uint16_t* x = input + c * 8;
+#define WF(i) oracle_bf16_to_f32(w[i])
+#define XF(i) oracle_bf16_to_f32(x[i])
+            d = fmaf(WF(0), XF(0), WF(1) * XF(1));
+            d = fmaf(WF(2), XF(2), fmaf(WF(3), XF(3), d));
+            d = fmaf(WF(4), XF(4), fmaf(WF(5), XF(5), d));
+            d = fmaf(WF(6), XF(6), fmaf(WF(7), XF(7), d));
+#undef WF
+#undef XF
+          }
+          sum += d;
+        }
+        lane_sum[l] = sum;
+      }
+      for (int off = 16; off > 0; off >>= 1) {
+        for (int i = 0; i < off; ++i) lane_sum[i] = lane_sum[i] + lane_sum[i + off];
+      }
+      partial[ws] = lane_sum[0];
+    }
+    float total;
+    if (wpr > 1) {
+      total = 0.0f;
+      for (int ws = 0; ws < wpr; ++ws) total += partial[ws];
+    } else {
+      total = partial[0];
+    }
+    const float b = bias ? oracle_bf16_to_f32(bias[r]) : 0.0f;
+    out[r] = oracle_f32_to_bf16(total + b);
+  }
+}

@@ -50,6 +50,7 @@ def lib():
         L.oracle_lm_head.argtypes = [_p, _p, _i, _p, _p, _p, _i, _i, _i]
         L.oracle_lm_head.restype = _i
         L.oracle_quantize_groupwise.argtypes = [_p, _i, _i, _i, _p, _p]
+        L.oracle_gemv_reference_order.argtypes = [_p, _i, _p, _p, _p, _p, _i, _i, _i]
         _LIB = L
     return _LIB
 
@@ -113,6 +114,22 @@ def lm_head(weight, bias, x, scales=None, group_size=64):
     idx = lib().oracle_lm_head(_ptr(weight), _ptr(s), group_size, _ptr(b), _ptr(x),
                                _ptr(logits), v, k, 1 if is8 else 0)
     return logits, int(idx)
+
+
+def gemv_reference_order(weight, bias, x, scales=None, lm_head=False) -> np.ndarray:
+    """BF16 bits of the decode GEMV (int8 weight => W8A16) or the BF16 LM-head
+    logits, computed in the reference CUDA kernels' own FP32 operation order
+    (src/cuda/kernels.cu:359-384, 438-603, 953-1041)."""
+    x = np.ascontiguousarray(x, dtype=np.uint16).reshape(-1)
+    is8 = weight.dtype == np.int8
+    weight = np.ascontiguousarray(weight)
+    n, k = weight.shape
+    out = np.empty(n, dtype=np.uint16)
+    s = None if scales is None else np.ascontiguousarray(scales, dtype=np.uint16)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.uint16)
+    lib().oracle_gemv_reference_order(_ptr(weight), 1 if is8 else 0, _ptr(s), _ptr(b),
+                                      _ptr(x), _ptr(out), n, k, 1 if lm_head else 0)
+    return out
 
 
 def quantize_groupwise(weight, group_size=64):

@@ -45,6 +45,8 @@ _SIGNATURES = {
     "b200_gemm_reserve_scratch": ([ctypes.c_size_t], _i),
     "b200_lm_head_noalloc_max_vocab": ([], ctypes.c_size_t),
     "b200_lm_head_bf16_noalloc": ([_p, _p, _p, _p, _p, _i, _i, _p], _i),
+    "b200_set_summation_order": ([_i], _i),
+    "b200_summation_order": ([], _i),
 }
 for _name, (_args, _res) in _SIGNATURES.items():
     _fn = getattr(_lib, _name)
@@ -59,6 +61,8 @@ B200_ERR_GROUP_SIZE = -2
 B200_ERR_WORKSPACE = -3
 B200_ERR_TOO_LARGE = -4
 B200_ERR_NCCL = -5
+ORDER_FAST = 0
+ORDER_REFERENCE = 1
 
 
 class Error(RuntimeError):
@@ -100,6 +104,20 @@ def version() -> int:
 def device_status(clear: bool = False) -> int:
     """Device-side error word (B200_DEVICE_*); synchronises the device."""
     return _lib.b200_device_status(1 if clear else 0)
+
+
+def set_summation_order(order) -> None:
+    """Decode GEMV / LM-head summation order: ORDER_FAST (default) or
+    ORDER_REFERENCE (every FP32 operation in the reference kernels' order;
+    bit-identical outputs on the reference's fast-path shapes).  Also accepts
+    "fast" / "reference".  Process-wide."""
+    if isinstance(order, str):
+        order = {"fast": ORDER_FAST, "reference": ORDER_REFERENCE}[order]
+    _check(_lib.b200_set_summation_order(int(order)), "set_summation_order")
+
+
+def summation_order() -> int:
+    return _lib.b200_summation_order()
 
 
 # ---------------------------------------------------------------- Linear API

@@ -104,7 +104,17 @@ int lm_head_common(bool w8, const void* weight, const uint16_t* scales,
 
 extern "C" {
 
-int b200_version(void) { return 100; }
+int b200_version(void) { return 200; }
+
+int b200_set_summation_order(int order) {
+  if (order != B200_ORDER_FAST && order != B200_ORDER_REFERENCE) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  b200::set_summation_order(order);
+  return B200_OK;
+}
+
+int b200_summation_order(void) { return b200::summation_order(); }
 
 const char* b200_status_string(int status) {
   switch (status) {

@@ -25,9 +25,13 @@
 // (lowest index on ties) written to the caller's workspace, and a one-CTA
 // reduction kernel (launched with PDL) that writes the final index.
 
+#include <atomic>
 #include <cfloat>
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 
+#include "b200_linear.h"
 #include "common.cuh"
 #include "gemv_math.cuh"
 #include "kernels.h"
@@ -390,6 +394,96 @@ argmax_bf16_kernel(const bf16* __restrict__ values, int n,
 // 4p..4p+3 of every chunk) so that consecutive lanes read consecutive
 // 16-byte words (no bank conflicts).  The INT8 products use the sm_100
 // packed FP32 instructions (2 elements per FADD2 / FFMA2).
+// ---------------------------------------------------------------------------
+// Reference summation order (opt-in, b200_set_summation_order).  The
+// reference decode kernels (src/cuda/kernels.cu:359-384, 438-490, 492-568,
+// 953-1041; built with --use_fast_math, so every FP32 add / mul / fma
+// flushes denormals) sum a row as follows: lane l of the row's warp(s)
+// walks chunks c = l + 32*ws, l + 32*ws + 32*W, ... (ws: the warp's slice of
+// a row split over W warps); each chunk's dot product is a fresh chain
+// (W8A16, 16 int8: d = fma(q0*s, x0, 0), d = fma(q_i*s, x_i, d) in element
+// order; BF16, 8 elements: d = fma(w0, x0, w1*x1), then
+// d = fma(w_2j, x_2j, fma(w_2j+1, x_2j+1, d)) for j = 1..3); the lane adds
+// its chunks in order to a sum that starts at 0; the warp reduces with
+// __shfl_down (offsets 16..1); split rows add the W warp partials in order
+// to 0; the bias is added and the result rounded to BF16.  The helpers below
+// compute two independent chunk chains at once (packed FP32x2, FTZ), which
+// is the same arithmetic per chain.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+  return (static_cast<unsigned long long>(__float_as_uint(v.y)) << 32) |
+         __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 bits_f2(unsigned long long b) {
+  return make_float2(__uint_as_float(uint32_t(b)), __uint_as_float(uint32_t(b >> 32)));
+}
+__device__ __forceinline__ float2 fma2_ftz(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;"
+      : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 mul2_ftz(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float add_ftz(float a, float b) {
+  float d;
+  asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+// Exact int8 -> FP32 of byte j of two words (biased by XOR 0x80 first).
+template <int kJ>
+__device__ __forceinline__ float2 s8_pair(uint32_t b0, uint32_t b1) {
+  constexpr uint32_t sel = 0x7540u + kJ;
+  return __fadd2_rn(f2(__uint_as_float(__byte_perm(b0, 0x4B000000u, sel)),
+                       __uint_as_float(__byte_perm(b1, 0x4B000000u, sel))),
+                    f2(-8388736.0f, -8388736.0f));
+}
+// W8A16: the reference chains of chunk words w0 (chain .x) and w1 (chain .y)
+// with x planes x0 / x1 and scales (s0, s1).  One 32-bit word = elements
+// 4p..4p+3 of a chunk (plane p).
+template <int kP>
+__device__ __forceinline__ float2 ref_w8_word(uint32_t w0, uint32_t w1, float4 x0,
+                                              float4 x1, float2 sc, float2 d) {
+  const uint32_t b0 = w0 ^ 0x80808080u, b1 = w1 ^ 0x80808080u;
+  const float2 q0 = mul2_ftz(s8_pair<0>(b0, b1), sc);
+  const float2 q1 = mul2_ftz(s8_pair<1>(b0, b1), sc);
+  const float2 q2 = mul2_ftz(s8_pair<2>(b0, b1), sc);
+  const float2 q3 = mul2_ftz(s8_pair<3>(b0, b1), sc);
+  d = fma2_ftz(q0, f2(x0.x, x1.x), d);
+  d = fma2_ftz(q1, f2(x0.y, x1.y), d);
+  d = fma2_ftz(q2, f2(x0.z, x1.z), d);
+  d = fma2_ftz(q3, f2(x0.w, x1.w), d);
+  return d;
+}
+__device__ __forceinline__ float2 ref_w8_chunks(uint4 w0, uint4 w1, const float4* x0,
+                                                const float4* x1, float2 sc) {
+  float2 d = f2(0.0f, 0.0f);
+  d = ref_w8_word<0>(w0.x, w1.x, x0[0], x1[0], sc, d);
+  d = ref_w8_word<1>(w0.y, w1.y, x0[1], x1[1], sc, d);
+  d = ref_w8_word<2>(w0.z, w1.z, x0[2], x1[2], sc, d);
+  d = ref_w8_word<3>(w0.w, w1.w, x0[3], x1[3], sc, d);
+  return d;
+}
+// BF16: the reference chains of two 8-element chunks.
+__device__ __forceinline__ float2 ref_bf16_chunks(uint4 w0, uint4 w1, const float4* x0,
+                                                  const float4* x1) {
+  const float2 wa0 = f2(bf16_lo(w0.x), bf16_lo(w1.x)), wb0 = f2(bf16_hi(w0.x), bf16_hi(w1.x));
+  const float2 wa1 = f2(bf16_lo(w0.y), bf16_lo(w1.y)), wb1 = f2(bf16_hi(w0.y), bf16_hi(w1.y));
+  const float2 wa2 = f2(bf16_lo(w0.z), bf16_lo(w1.z)), wb2 = f2(bf16_hi(w0.z), bf16_hi(w1.z));
+  const float2 wa3 = f2(bf16_lo(w0.w), bf16_lo(w1.w)), wb3 = f2(bf16_hi(w0.w), bf16_hi(w1.w));
+  float2 d = mul2_ftz(wb0, f2(x0[0].y, x1[0].y));
+  d = fma2_ftz(wa0, f2(x0[0].x, x1[0].x), d);
+  d = fma2_ftz(wb1, f2(x0[0].w, x1[0].w), d);
+  d = fma2_ftz(wa1, f2(x0[0].z, x1[0].z), d);
+  d = fma2_ftz(wb2, f2(x0[1].y, x1[1].y), d);
+  d = fma2_ftz(wa2, f2(x0[1].x, x1[1].x), d);
+  d = fma2_ftz(wb3, f2(x0[1].w, x1[1].w), d);
+  d = fma2_ftz(wa3, f2(x0[1].z, x1[1].z), d);
+  return d;
+}
+
 constexpr int kConsumerWarps = 16;
 constexpr int kBulkThreads = 32 * (kConsumerWarps + 1);
 constexpr int kBulkSmemBudget = 200 * 1024;
@@ -408,7 +502,8 @@ static __device__ int g_gemv_status = 0;
 // kK != 0 compiles the kernel for that in_features (the Qwen2.5 hidden size
 // 896): the chunk loop is fully unrolled and every shared-memory offset is
 // an immediate.  kK == 0 handles any in_features.
-template <bool kW8, int kLPR, int kR, int kWPR, int kK>
+// kRef: the reference summation order above (kLPR == 32, kR == 1).
+template <bool kW8, int kLPR, int kR, int kWPR, int kK, bool kRef>
 __global__ void __launch_bounds__(kBulkThreads, 1)
 gemv_bulk_kernel(const void* __restrict__ weight,
                  const bf16* __restrict__ scales,
@@ -420,6 +515,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   constexpr int kEPC = kW8 ? 16 : 8;  // elements per 16-byte chunk
   constexpr int kPlanes = kEPC / 4;
   static_assert(kWPR == 1 || (kLPR == 32 && kR == 1), "split rows use whole warps");
+  static_assert(!kRef || (kLPR == 32 && kR == 1), "reference order: one row per warp");
   constexpr int kGroups = kWPR > 1 ? 1 : 32 / kLPR;  // row groups per warp
   constexpr int kWarpRows = kGroups * kR;
   constexpr int kTileRows =
@@ -590,7 +686,32 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         }
       };
       const int c0 = ok ? ksub * kLPR + ll : chunks;  // failed: no chunks
-      if constexpr (kK != 0) {
+      float ref_sum = 0.0f;
+      if constexpr (kRef) {
+        // Chunks c0, c0 + kSpan, ... in pairs; the lane sum adds them in order.
+        const int rl = rloc0;
+        for (int c = c0; c < chunks; c += 2 * kSpan) {
+          const int c1 = c + kSpan < chunks ? c + kSpan : c;
+          float4 x0[kPlanes], x1[kPlanes];
+#pragma unroll
+          for (int p = 0; p < kPlanes; ++p) {
+            x0[p] = xs[p * chunks + c];
+            x1[p] = xs[p * chunks + c1];
+          }
+          const uint4 w0 = *reinterpret_cast<const uint4*>(wt + rl * row_bytes + c * 16);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(wt + rl * row_bytes + c1 * 16);
+          float2 d;
+          if constexpr (kW8) {
+            const float2 sc = f2(__bfloat162float(stile[rl * groups + (c >> 2)]),
+                                 __bfloat162float(stile[rl * groups + (c1 >> 2)]));
+            d = ref_w8_chunks(w0, w1, x0, x1, sc);
+          } else {
+            d = ref_bf16_chunks(w0, w1, x0, x1);
+          }
+          ref_sum = add_ftz(ref_sum, d.x);
+          if (c1 != c) ref_sum = add_ftz(ref_sum, d.y);
+        }
+      } else if constexpr (kK != 0) {
 #pragma unroll
         for (int j = 0; j < kIters; ++j) {
           const int c = c0 + j * kSpan;
@@ -605,10 +726,20 @@ gemv_bulk_kernel(const void* __restrict__ weight,
       const int row0 = tile * kTileRows + rloc0;
 #pragma unroll
       for (int r = 0; r < kR; ++r) {
-        float v = acc2[r].x + acc2[r].y;
+        float v;
+        if constexpr (kRef) {
+          // Same tree as the reference's __shfl_down reduction at lane 0.
+          v = ref_sum;
 #pragma unroll
-        for (int off = kLPR / 2; off > 0; off >>= 1) {
-          v += __shfl_xor_sync(0xffffffffu, v, off);
+          for (int off = 16; off > 0; off >>= 1) {
+            v = add_ftz(v, __shfl_xor_sync(0xffffffffu, v, off));
+          }
+        } else {
+          v = acc2[r].x + acc2[r].y;
+#pragma unroll
+          for (int off = kLPR / 2; off > 0; off >>= 1) {
+            v += __shfl_xor_sync(0xffffffffu, v, off);
+          }
         }
         if constexpr (kWPR > 1) {
           // Partials of the kWPR warps of a row meet in shared memory
@@ -619,13 +750,15 @@ gemv_bulk_kernel(const void* __restrict__ weight,
           if (ksub == 0) {
             v = 0.0f;
 #pragma unroll
-            for (int j = 0; j < kWPR; ++j) v += part[cw + j];
+            for (int j = 0; j < kWPR; ++j) {
+              v = kRef ? add_ftz(v, part[cw + j]) : v + part[cw + j];
+            }
           }
         }
         const int row = row0 + r;
         if (ok && ll == 0 && ksub == 0 && row < n_rows) {
           const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
-          const bf16 y = __float2bfloat16_rn(v + b);
+          const bf16 y = __float2bfloat16_rn(kRef ? add_ftz(v, b) : v + b);
           if (fusion.residual != nullptr) {
             fusion.residual[row] = __float2bfloat16_rn(
                 __bfloat162float(fusion.residual[row]) + __bfloat162float(y));
@@ -669,6 +802,7 @@ struct BulkPlan {
   int w_tile_bytes = 0;
   int smem = 0;
   int grid = 0;
+  bool ref = false;  // reference summation order (kLPR 32, kR 1)
 };
 
 int device_sm_count() {
@@ -729,13 +863,43 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   return best;
 }
 
-template <bool kW8, int kLPR, int kR, int kWPR>
+// Reference-order plan: one warp per row (the row split over 4 warps when
+// the reference splits it: a GEMV with in_features > 1024), 16 or 4 rows per
+// tile, as many stages as fit.
+BulkPlan plan_bulk_ref(bool w8, int n, int k, bool lm_head) {
+  BulkPlan p;
+  const int sms = device_sm_count();
+  const int wpr = (k > 1024 && (w8 || !lm_head)) ? 4 : 1;
+  const int rows = kConsumerWarps / wpr;
+  const int row_bytes = w8 ? k : 2 * k;
+  const int groups = (k + 63) / 64;
+  const int budget = kBulkSmemBudget - k * 4 - 512;
+  const int st = (rows * row_bytes + (w8 ? rows * groups * 2 : 0) + 127) / 128 * 128;
+  const int stages = budget / st < 16 ? budget / st : 16;
+  if (stages < 2) return p;
+  const int tiles = (n + rows - 1) / rows;
+  int grid = tiles < sms ? tiles : sms;
+  if (lm_head && grid > (n + 7) / 8) grid = (n + 7) / 8;  // ceil(n/8) partials
+  p.lpr = 32;
+  p.r = 1;
+  p.wpr = wpr;
+  p.stages = stages;
+  p.stage_bytes = st;
+  p.w_tile_bytes = rows * row_bytes;
+  p.smem = stages * st + k * 4 + 8 * 2 * stages + 8 + 8 * kConsumerWarps +
+           8 * kConsumerWarps + 4 * kConsumerWarps;
+  p.grid = grid;
+  p.ref = true;
+  return p;
+}
+
+template <bool kW8, int kLPR, int kR, int kWPR, bool kRef = false>
 cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                         const bf16* b, const bf16* x, bf16* y, int n, int k,
                         float* bv, int* bi, cudaStream_t stream,
                         const GemvFusion& fusion) {
-  auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896>
-                         : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0>;
+  auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef>
+                         : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef>;
   cudaError_t e = cudaFuncSetAttribute(
       kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
   if (e != cudaSuccess) return e;
@@ -757,6 +921,11 @@ template <bool kW8>
 cudaError_t dispatch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                           const bf16* b, const bf16* x, bf16* y, int n, int k,
                           float* bv, int* bi, cudaStream_t st, const GemvFusion& f) {
+  if (p.ref) {
+    return p.wpr == 4
+               ? launch_bulk<kW8, 32, 1, 4, true>(p, w, s, b, x, y, n, k, bv, bi, st, f)
+               : launch_bulk<kW8, 32, 1, 1, true>(p, w, s, b, x, y, n, k, bv, bi, st, f);
+  }
   if (p.wpr == 4) return launch_bulk<kW8, 32, 1, 4>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   if (p.wpr == 2) return launch_bulk<kW8, 32, 1, 2>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   if (p.lpr == 8) {
@@ -880,10 +1049,30 @@ struct GemvPlan {
 
 int stream_rows_per_block(int tpr, int r) { return (kThreads / tpr) * r; }
 
+// The reference's own fast-path conditions (src/cuda/kernels.cu:1540-1579,
+// 1627-1655): outside them it runs other kernels, whose order the reference
+// mode does not reproduce.
+bool reference_fast_shape(bool w8, const void* weight, const void* input, int k,
+                          bool lm_head) {
+  if (!aligned16(weight) || !aligned16(input)) return false;
+  if (w8) return k >= 16 && k % 64 == 0;
+  return lm_head ? k % 8 == 0 && k > 0 : k >= 8 && k % 8 == 0;
+}
+
 GemvPlan plan_gemv(bool w8, const void* weight, const bf16* scales, int n,
-                   int k, const void* input, bool lm_head) {
+                   int k, const void* input, bool lm_head, bool fused = false) {
   GemvPlan plan;
   if (n <= 0) return plan;
+  if (!fused && summation_order() == B200_ORDER_REFERENCE &&
+      reference_fast_shape(w8, weight, input, k, lm_head) && n % 8 == 0 &&
+      (!w8 || aligned16(scales)) && k <= 32768) {
+    plan.bulk = plan_bulk_ref(w8, n, k, lm_head);
+    if (plan.bulk.lpr > 0) {
+      plan.kind = 2;
+      plan.grid = plan.bulk.grid;
+      return plan;
+    }
+  }
   if (!gemv_uses_fast_path(w8, weight, input, k)) {
     plan.kind = 1;
     plan.grid = (n + 7) / 8;
@@ -911,6 +1100,28 @@ GemvPlan plan_gemv(bool w8, const void* weight, const bf16* scales, int n,
 
 }  // namespace
 
+namespace {
+// -1: not read yet from B200_SUMMATION_ORDER.
+std::atomic<int> g_summation_order{-1};
+}  // namespace
+
+int summation_order() {
+  int v = g_summation_order.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = getenv("B200_SUMMATION_ORDER");
+    v = (e != nullptr && strcmp(e, "reference") == 0) ? B200_ORDER_REFERENCE
+                                                      : B200_ORDER_FAST;
+    int expected = -1;
+    g_summation_order.compare_exchange_strong(expected, v);
+    v = g_summation_order.load(std::memory_order_relaxed);
+  }
+  return v;
+}
+
+void set_summation_order(int order) {
+  g_summation_order.store(order, std::memory_order_relaxed);
+}
+
 int gemv_grid(bool w8, const void* weight, const bf16* scales,
               const void* input, int n, int k, bool lm_head) {
   return plan_gemv(w8, weight, scales, n, k, input, lm_head).grid;
@@ -926,7 +1137,7 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
   const bool fused = fusion != nullptr &&
                      (f.in_mode != 0 || f.residual != nullptr);
   const GemvPlan plan =
-      plan_gemv(w8, weight, scales, n, k, input, block_value != nullptr);
+      plan_gemv(w8, weight, scales, n, k, input, block_value != nullptr, fused);
   if (grid_out) *grid_out = plan.grid;
   if (plan.kind == 0) return cudaSuccess;
   // The fusions exist only in the TMA-bulk kernel.

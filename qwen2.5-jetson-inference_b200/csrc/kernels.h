@@ -24,6 +24,11 @@ struct GemvFusion {
 };
 
 // gemv.cu
+// Summation order of the decode GEMV / LM head (B200_ORDER_FAST or
+// B200_ORDER_REFERENCE); process-wide, initialised from the environment
+// variable B200_SUMMATION_ORDER ("reference" or "fast").
+int summation_order();
+void set_summation_order(int order);
 bool gemv_uses_fast_path(bool w8, const void* weight, const void* input,
                          int k);
 // CTA count launch_gemv will use for these arguments (lm_head: the form with

@@ -53,7 +53,9 @@ def run(kind: str, model_dir: str, prompt: list[int], backend: str = "cuda",
         precision: str = "w16a16", linear_kernel: str = "custom", new_tokens: int = 128,
         warmup: int = 5, repeat: int = 20, max_seq_len: int = 256,
         logits_out: str | None = None, force_tokens: list[int] | None = None,
-        timeout: int = 1800) -> dict:
+        timeout: int = 1800, summation_order: str | None = None) -> dict:
+    """Runs one binary; summation_order ("reference" / "fast") sets the b200
+    library's decode summation order (B200_SUMMATION_ORDER) for that run."""
     cmd = [binary(kind), "--model", model_dir, "--backend", backend, "--precision",
            precision, "--linear-kernel", linear_kernel, "--token-ids",
            ",".join(map(str, prompt)), "--new-tokens", str(new_tokens), "--warmup",
@@ -62,7 +64,10 @@ def run(kind: str, model_dir: str, prompt: list[int], backend: str = "cuda",
         cmd += ["--logits-out", logits_out]
     if force_tokens:
         cmd += ["--force-tokens", ",".join(map(str, force_tokens))]
-    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
+    env = dict(os.environ)
+    if summation_order is not None:
+        env["B200_SUMMATION_ORDER"] = summation_order
+    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
     if proc.returncode != 0:
         raise RuntimeError(f"{' '.join(cmd[:2])} failed: {proc.stderr[-2000:]}")
     return json.loads(proc.stdout.strip().splitlines()[-1])

@@ -72,3 +72,35 @@ def test_teacher_forced_disagreements_are_near_ties(e2e, precision):
     top = max(abs(g) for g in ours["forced_gap"]) if ours["forced_gap"] else 0
     for g in res["disagree_gaps"]:
         assert g <= 0.0625, res  # <= 2 BF16 ulps for logits in [2, 4)
+
+
+@pytest.fixture(scope="module")
+def e2e24(b200, cuda):
+    m = importlib.import_module("qwen25_b200.e2e")
+    q = importlib.import_module("qwen25_b200.qbin")
+    try:
+        m.binary("b200"), m.binary("reference")
+    except FileNotFoundError as e:
+        pytest.skip(str(e))
+    m.ensure_model(MODEL24_DIR, dict(q.QWEN25_05B), seed=0,
+                   precisions=("w16a16", "w8a16"))
+    return m
+
+
+MODEL24_DIR = "/tmp/b200_e2e_qwen2_24layer_w"
+
+
+@pytest.mark.parametrize("precision", ["w16a16", "w8a16"])
+def test_configs3_tokens_identical_in_reference_order(e2e24, precision):
+    """the full 24-layer synthetic Qwen2.5-0.5B, 32-token prompt,
+    128 greedy tokens.  With the library in reference summation order the
+    reference engine produces the SAME 128 token ids with the b200 Linear
+    kernels as with its own (the north-star equivalence criterion); the
+    prefill GEMMs already agree bit for bit in either order."""
+    prompt = e2e24.prompt_ids(32, seed=0)
+    ours = e2e24.run("b200", MODEL24_DIR, prompt, precision=precision, new_tokens=128,
+                     warmup=0, repeat=1, summation_order="reference")
+    ref = e2e24.run("reference", MODEL24_DIR, prompt, precision=precision,
+                    new_tokens=128, warmup=0, repeat=1)
+    assert len(ref["tokens"]) == 128
+    assert ours["tokens"] == ref["tokens"]

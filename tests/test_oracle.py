@@ -3,6 +3,8 @@
 Golden fixtures come from the reference's own exporter and its CPU FP32
 Linear (tests/golden/make_golden.py); the known answers below are the
 reference exporter's self-test values (tools/export_model.py:414-428)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -75,3 +77,19 @@ def test_argmax_ties_and_degenerate(oracle):
     v = oracle.f32_to_bf16(np.array([-np.inf, np.nan, -np.inf], np.float32))
     assert oracle.argmax_bf16(v) == 0
     assert oracle.argmax_bf16(np.zeros(0, np.uint16)) == 0
+
+
+def test_reference_order_matches_reference_cuda_kernels(oracle):
+    """The CPU restatement of the reference decode kernels' FP32 operation
+    order (oracle_gemv_reference_order) against outputs of the reference's
+    own CUDA kernels, bit for bit (fixture made on a B200 by
+    tests/golden/make_ref_kernel_golden.py)."""
+    from golden.make_ref_kernel_golden import REF_ORDER_CASES, ref_order_inputs
+    path = os.path.join(os.path.dirname(__file__), "golden", "ref_kernels_order.npz")
+    if not os.path.exists(path):
+        pytest.skip("ref_kernels_order.npz not generated yet")
+    g = np.load(path)
+    for i, (name, kind, n, k) in enumerate(REF_ORDER_CASES):
+        w, s, b, x = ref_order_inputs(kind, n, k, 100 + i)
+        got = oracle.gemv_reference_order(w, b, x, scales=s, lm_head=(kind == "lm"))
+        assert np.array_equal(got, g[name]), name

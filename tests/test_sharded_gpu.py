@@ -1,6 +1,7 @@
 """Sharded Linear on the GPU: the single-rank communicator on any box, and a
 torchrun job over every visible GPU (2..8) when the box has several."""
 import os
+import re
 import socket
 import subprocess
 import sys
@@ -98,7 +99,8 @@ def _run_worker(nproc, shapes):
            os.path.join(REPO, "tests", "sharded_worker.py"), "--shapes", shapes]
     proc = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
-    assert proc.stdout.count(" ok") == nproc, proc.stdout[-3000:]
+    done = re.findall(r"^rank \d+ ok$", proc.stdout, flags=re.M)
+    assert len(done) == nproc, proc.stdout[-3000:]
     return proc.stdout
 
 
