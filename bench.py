@@ -438,17 +438,21 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
         return {"unavailable": str(err)}
     model = e2e.ensure_model("/tmp/b200_e2e_qwen2_05b", dict(q.QWEN25_05B), seed=0)
     prompt = e2e.prompt_ids(32, seed=0)
-    runs = [("b200", "w8a16", "custom"), ("b200", "w16a16", "custom"),
-            ("reference", "w8a16", "custom"), ("reference", "w16a16", "custom"),
-            ("reference", "w16a16", "cublas")]
+    # (linear kernels, precision, --linear-kernel, b200 summation order)
+    runs = [("b200", "w8a16", "custom", "fast"), ("b200", "w16a16", "custom", "fast"),
+            ("b200", "w8a16", "custom", "reference"),
+            ("b200", "w16a16", "custom", "reference"),
+            ("reference", "w8a16", "custom", None), ("reference", "w16a16", "custom", None),
+            ("reference", "w16a16", "cublas", None)]
     out = {"prompt_tokens": 32, "new_tokens": new_tokens, "runs": []}
     tokens = {}
-    for kind, prec, lk in runs:
+    for kind, prec, lk, order in runs:
         r = e2e.run(kind, model, prompt, precision=prec, linear_kernel=lk,
-                    new_tokens=new_tokens, warmup=warmup, repeat=repeat)
-        tokens[(kind, prec, lk)] = r["tokens"]
+                    new_tokens=new_tokens, warmup=warmup, repeat=repeat,
+                    summation_order=order)
+        tokens[(kind, prec, lk, order)] = r["tokens"]
         out["runs"].append({
-            "linear": kind, "precision": prec, "linear_kernel": lk,
+            "linear": kind, "precision": prec, "linear_kernel": lk, "order": order,
             "decode_tok_s": round(statistics.median(r["decode_tok_s"]), 1),
             "ttft_ms": round(statistics.median(r["ttft_ms"]), 3),
             "tpot_ms": round(statistics.median(r["tpot_ms"]), 4)})
@@ -456,17 +460,21 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
         return next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
 
     for prec in ("w8a16", "w16a16"):
-        ref = tokens[("reference", prec, "custom")]
-        out[f"token_identical_prefix_{prec}"] = prefix(tokens[("b200", prec, "custom")], ref)
+        ref = tokens[("reference", prec, "custom", None)]
+        out[f"token_identical_prefix_{prec}"] = prefix(
+            tokens[("b200", prec, "custom", "fast")], ref)
+        # the north-star criterion: reference summation order, all 128 tokens
+        out[f"token_identical_{prec}_reference_order"] = \
+            f"{prefix(tokens[('b200', prec, 'custom', 'reference')], ref)}/{len(ref)}"
         # Teacher-forced: fed the reference kernels' tokens, where do the b200
         # kernels pick another token, and how close were our top two logits?
         forced = e2e.run("b200", model, prompt, precision=prec, new_tokens=2, warmup=0,
                          repeat=1, force_tokens=ref)
         out[f"teacher_forced_{prec}"] = e2e.forced_agreement(forced, ref)
     # Control: the reference's own custom kernels against its own cuBLAS path.
-    cub = tokens[("reference", "w16a16", "cublas")]
+    cub = tokens[("reference", "w16a16", "cublas", None)]
     out["reference_custom_vs_cublas_prefix_w16a16"] = prefix(
-        tokens[("reference", "w16a16", "custom")], cub)
+        tokens[("reference", "w16a16", "custom", None)], cub)
     forced = e2e.run("reference", model, prompt, precision="w16a16", new_tokens=2,
                      warmup=0, repeat=1, force_tokens=cub)
     out["reference_custom_vs_cublas_teacher_forced_w16a16"] = e2e.forced_agreement(forced, cub)
@@ -481,7 +489,7 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
                 eng.generate(prompt, new_tokens)
             runs = [eng.generate(prompt, new_tokens) for _ in range(repeat)]
             toks = runs[0][0]
-            ref = tokens[("reference", prec, "custom")]
+            ref = tokens[("reference", prec, "custom", None)]
             am, gaps = eng.teacher_forced(prompt, ref)
             dis = [j for j in range(len(ref)) if am[j] != ref[j]]
             out["native_engine"].append({
@@ -495,6 +503,8 @@ def e2e_bench(new_tokens=128, warmup=2, repeat=5):
                     "disagree_gaps": [round(gaps[j], 5) for j in dis]},
                 "device_status": eng.device_status()})
             eng.close()
+    out["runs"] = table(out["runs"], ["linear", "precision", "linear_kernel", "order",
+                                      "decode_tok_s", "ttft_ms", "tpot_ms"])
     cpu = e2e.run("reference", model, prompt, backend="cpu", precision="fp32",
                   new_tokens=16, warmup=0, repeat=1)
     out["cpu_fp32"] = {"decode_tok_s": round(cpu["decode_tok_s"][0], 2),
@@ -549,6 +559,11 @@ def cpu_reference_sample(steps, warmup, budget_s=12.0, min_s=0.0):
 
 
 # ------------------------------------------------------------------- main
+def table(rows, cols):
+    """List of dicts -> {"cols": [...], "rows": [[...], ...]} (compact JSON)."""
+    return {"cols": cols, "rows": [[r[c] for c in cols] for r in rows]}
+
+
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -878,13 +893,16 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,
-            "sweep_w8a16": shapes_w8,
-            "sweep_bf16": shapes_bf16,
-            "gemm_sweep": gemm,
-            "sharded": sharded,
-            "e2e_decode": e2e_decode,
             "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf_burst,
                       "bf16_tflops_sustained": tf_sust, "kind": peak_kind},
+            "sweep_w8a16": table(shapes_w8, ["k", "n", "us", "gbs"]),
+            "sweep_bf16": table(shapes_bf16, ["k", "n", "us", "gbs"]),
+            "gemm_sweep": None if gemm is None else table(
+                gemm, ["w8", "m", "k", "n", "us", "tflops"]),
+            # the end of the line survives in truncated logs: keep the
+            # multi-GPU and end-to-end results last
+            "e2e_decode": e2e_decode,
+            "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
