@@ -348,7 +348,7 @@ def sharded_bench(b200, world, rank, device, reps=5):
             res[name + "_ms"] = round(t * 1e3, 3)
         res["tflops"] = round(2.0 * m * n * k / (res["sharded_ms"] / 1e3) / 1e12, 1)
         res["tflops_fused_p2p"] = round(2.0 * m * n * k / (res["fused_p2p_ms"] / 1e3) / 1e12, 1)
-        del ws, yl
+        del yl
         torch.cuda.empty_cache()
         if world > 1:
             # the same whole GEMM on one GPU, timed in this run (every rank
@@ -381,7 +381,7 @@ def sharded_bench(b200, world, rank, device, reps=5):
         checks.append(ok)
         out["gemm"].append(res)
         win.close()
-        del q, s, x, y
+        del q, s, x, y, ws
         torch.cuda.empty_cache()
     v, k = 151936, 896
     v0, vn = sh.shard_range(v, world, rank)

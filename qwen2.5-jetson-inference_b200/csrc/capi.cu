@@ -10,6 +10,7 @@ namespace b200 {
 cudaError_t read_device_status(int* value, bool clear);  // gemm_sm100.cu
 cudaError_t read_gemv_status(int* value, bool clear);    // gemv.cu
 cudaError_t read_comm_status(int* value, bool clear);    // sharded.cu
+cudaError_t read_w8t_status(int* value, bool clear);     // gemm_w8t.cu
 }
 
 using b200::bf16;
@@ -131,12 +132,13 @@ const char* b200_status_string(int status) {
 }
 
 int b200_device_status(int clear) {
-  int gemm = 0, gemv = 0, comm = 0;
+  int gemm = 0, gemv = 0, comm = 0, w8t = 0;
   cudaError_t e = b200::read_device_status(&gemm, clear != 0);  // synchronises
   if (e == cudaSuccess) e = b200::read_gemv_status(&gemv, clear != 0);
   if (e == cudaSuccess) e = b200::read_comm_status(&comm, clear != 0);
+  if (e == cudaSuccess) e = b200::read_w8t_status(&w8t, clear != 0);
   if (e != cudaSuccess) return -int(e);
-  return gemm != 0 ? gemm : gemv != 0 ? gemv : comm;
+  return gemm != 0 ? gemm : gemv != 0 ? gemv : comm != 0 ? comm : w8t;
 }
 
 int b200_gemv_bf16(const uint16_t* weight, const uint16_t* bias,

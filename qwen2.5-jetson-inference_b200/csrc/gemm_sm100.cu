@@ -42,6 +42,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace b200 {
 
@@ -69,62 +70,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           int error_code) {
   return mbar_wait_bounded(bar, parity, abort_flag, error_code,
                            &g_device_status);
-}
-
-// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
-// layout written by TMA SWIZZLE_128B: rows of 128 bytes, 8-row (1024-byte)
-// swizzle atoms stacked along M/N (stride byte offset 1024), descriptor
-// version 1 (sm_100), layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
-  uint64_t d = 0;
-  d |= uint64_t((addr & 0x3FFFFu) >> 4);
-  d |= uint64_t(1) << 16;              // leading byte offset (unused here)
-  d |= uint64_t(1024 >> 4) << 32;      // stride byte offset
-  d |= uint64_t(1) << 46;              // version
-  d |= uint64_t(2) << 61;              // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor, kind::f16: D=F32, A=B=BF16, both K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) |
-         (uint32_t(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc,
-                                         uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
-          d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-      "[%0];" ::"r"(bar)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
-      "[%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
-        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
-        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-        "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // --------------------------------------------------------------- the kernel
@@ -1238,6 +1183,13 @@ cudaError_t launch_tile(Tile t, const void* weight, const bf16* scales,
 
 }  // namespace
 
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                    int elem_bytes, int inner, int outer, int box_inner, int box_outer,
+                    CUtensorMapSwizzle swizzle) {
+  return make_tmap_cached(map, base, dtype, elem_bytes, inner, outer, box_inner, box_outer,
+                          swizzle);
+}
+
 bool gemm_tc_supported(bool w8, const void* weight, const void* input,
                        const void* output, int m, int n, int k) {
   (void)output;
@@ -1365,6 +1317,16 @@ cudaError_t gemm_w8_two_pass(const void* weight, const bf16* scales, const bf16*
 
 }  // namespace
 
+// W8A16 prefill through the TMEM-resident dequantised weights
+// (gemm_w8t.cu); B200_GEMM_W8T=1 selects it.
+bool use_w8t() {
+  static const bool on = [] {
+    const char* e = getenv("B200_GEMM_W8T");
+    return e != nullptr && strcmp(e, "1") == 0;
+  }();
+  return on;
+}
+
 cudaError_t reserve_gemm_scratch(size_t bytes) {
   Scratch sc;
   return scratch_get(bytes == 0 ? kScratchCap : bytes, true, &sc);
@@ -1374,6 +1336,9 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
+  if (w8 && peers.n == 0 && use_w8t() && gemm_w8t_supported(weight, input, output, m, n, k)) {
+    return launch_gemm_w8t(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  }
   if (w8 && (m >= kTwoPassMinTokens ||
              (m <= kTwoPassMaxFewTokens && k >= kTwoPassFewTokensMinK)) &&
       !getenv("B200_GEMM_ONE_PASS")) {

@@ -1,0 +1,435 @@
+// W8A16 prefill GEMM with the dequantised weights held in TENSOR MEMORY.
+//
+//   Y[M,N] = bf16( X[M,K] . bf16(q[N,K] * s[N,K/64])^T + b[N] )
+//
+// computed as its transpose, Y^T = W . X^T, so that the weight tile is the
+// MMA's A operand and can live in TMEM instead of shared memory:
+//   * TMA brings raw INT8 weight tiles [128 rows x 64] (64-byte swizzle) and
+//     X tiles [kBT tokens x 64] BF16 (128-byte swizzle) into a shared-memory
+//     ring;
+//   * eight dequantiser warps turn each INT8 tile into bf16(q*s) in
+//     registers and write it with tcgen05.st into a ring of A slots in TMEM
+//     (row r of the tile = TMEM lane r; 64 K values = 32 columns of BF16
+//     pairs).  The dequantised weights never touch shared memory: per k-block
+//     the SMEM traffic is the X tile (TMA write + MMA read) plus the 8 KB INT8
+//     tile, instead of also writing and reading a 16 KB BF16 weight tile;
+//   * one thread issues tcgen05.mma.cta_group::1.kind::f16 with A from TMEM
+//     and B (= the X tile, K-major) from shared memory: D[128 x kBT] FP32 in
+//     TMEM, double-buffered across tiles;
+//   * four epilogue warps read D with tcgen05.ld (lane = output feature n,
+//     column = token), add the bias (one value per thread), round to BF16
+//     and store Y rows (pairs of features exchanged between neighbouring
+//     lanes so every store is 4 bytes and a warp writes two 64-byte row
+//     segments).
+//
+// The BF16 rounding of q*s and the K order (16 at a time, k ascending) are
+// those of the reference's tensor-core GEMM (src/cuda/kernels.cu:1075-1094,
+// 1096-1322), so results equal the other GEMM paths of this library.
+//
+// TMEM: 512 columns = 2 accumulators of kBT columns + kAStages A slots of 32.
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 4..7 epilogue,
+// 8..15 dequantisers (warp w reaches TMEM lanes 32*(w%4)..+31; warps w and
+// w+4 split the 64 K values of a k-block).  Every wait is bounded and
+// reports B200_DEVICE_TIMEOUT_* like the other GEMM kernels.  No multicast.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace b200 {
+
+__device__ int g_w8t_status = 0;
+
+cudaError_t read_w8t_status(int* value, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_w8t_status, sizeof(int));
+  if (e != cudaSuccess || !clear) return e;
+  const int zero = 0;
+  return cudaMemcpyToSymbol(g_w8t_status, &zero, sizeof(int));
+}
+
+// Tensor-map encoder with the per-call cache (gemm_sm100.cu).
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                    int elem_bytes, int inner, int outer, int box_inner, int box_outer,
+                    CUtensorMapSwizzle swizzle);
+
+namespace {
+
+constexpr int kRows = 128;   // weight rows (output features) per tile
+constexpr int kBK = 64;      // K per k-block = one quantisation group
+template <int kBT, int kGroups>
+struct CfgT {
+  static constexpr int kDqWarps = 4 * kGroups;            // one per lane quarter
+
+  static constexpr int kXBytes = kBT * kBK * 2;           // tokens x 64 BF16
+  static constexpr int kQBytes = kRows * kBK;             // 128 x 64 INT8
+  static constexpr int kStageBytes = kXBytes + kQBytes;
+  static constexpr int kStages =
+      (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+  static constexpr int kAccCols = kBT;
+  static constexpr int kACols = kBK / 2;                  // 32 columns / slot
+  static constexpr int kAStages =
+      (512 - 2 * kAccCols) / kACols > 8 ? 8 : (512 - 2 * kAccCols) / kACols;
+  static constexpr int kACol0 = 2 * kAccCols;
+  static constexpr int kThreads = (8 + kDqWarps) * 32;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+  static_assert(kBT % 16 == 0 && kBT >= 16 && kBT <= 256, "MMA N");
+  static_assert(kAStages >= 2, "TMEM: room for at least two A slots");
+  static_assert(kXBytes % 1024 == 0, "128B-swizzle atoms");
+};
+
+__device__ __forceinline__ bool wait_t(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                       int code) {
+  return mbar_wait_bounded(bar, parity, abort_flag, code, &g_w8t_status);
+}
+
+// bf16(q * s) of the four int8 of `word` -> two packed BF16 pairs.
+__device__ __forceinline__ void dq4(uint32_t word, bf162 s2, uint32_t* out) {
+  const uint32_t b = word ^ 0x80808080u;
+  const float2 q01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7540u)),
+                                            __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7541u))),
+                                make_float2(-8388736.0f, -8388736.0f));
+  const float2 q23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7542u)),
+                                            __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7543u))),
+                                make_float2(-8388736.0f, -8388736.0f));
+  // q has <= 8 significant bits: its BF16 is the top half of the float.
+  uint32_t p01 = __byte_perm(__float_as_uint(q01.x), __float_as_uint(q01.y), 0x7632);
+  uint32_t p23 = __byte_perm(__float_as_uint(q23.x), __float_as_uint(q23.y), 0x7632);
+  const bf162 neg0 = __halves2bfloat162(__ushort_as_bfloat16(0x8000), __ushort_as_bfloat16(0x8000));
+  // q*s is exact in FP32; fma.rn.bf16x2(q, s, -0) rounds it to BF16 once.
+  const bf162 d01 = __hfma2(*reinterpret_cast<bf162*>(&p01), s2, neg0);
+  const bf162 d23 = __hfma2(*reinterpret_cast<bf162*>(&p23), s2, neg0);
+  out[0] = *reinterpret_cast<const uint32_t*>(&d01);
+  out[1] = *reinterpret_cast<const uint32_t*>(&d23);
+}
+
+template <int kBT, int kGroups>
+__global__ void __launch_bounds__(CfgT<kBT, kGroups>::kThreads, 1)
+gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                const __grid_constant__ CUtensorMap tmap_q,
+                const uint16_t* __restrict__ scales, const bf16* __restrict__ bias,
+                bf16* __restrict__ out, int m, int n, int k, int ldc) {
+  using C = CfgT<kBT, kGroups>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  // full[S], empty[S], a_full[A], a_empty[A], acc_full[2], acc_empty[2]
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_empty = bar_full + 8 * C::kStages;
+  const uint32_t bar_afull = bar_empty + 8 * C::kStages;
+  const uint32_t bar_aempty = bar_afull + 8 * C::kAStages;
+  const uint32_t bar_acc_full = bar_aempty + 8 * C::kAStages;
+  const uint32_t bar_acc_empty = bar_acc_full + 16;
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 2 * C::kAStages + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (m + kBT - 1) / kBT;
+  const int num_n = (n + kRows - 1) / kRows;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (k + kBK - 1) / kBK;
+  const int groups = (k + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1 + 4);  // MMA commit + one dequant group
+    }
+    for (int a = 0; a < C::kAStages; ++a) {
+      mbar_init(bar_afull + 8 * a, 4);
+      mbar_init(bar_aempty + 8 * a, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_acc_full + 8 * b, 1);
+      mbar_init(bar_acc_empty + 8 * b, 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile % num_m;
+        const int nb = tile / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_t(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                      B200_DEVICE_TIMEOUT_PIPELINE))
+            goto producer_done;
+          unsigned char* st = smem + stage * C::kStageBytes;
+          const uint32_t fb = bar_full + 8 * stage;
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          tma_load_2d(smem_u32(st), &tmap_x, kb * kBK, mb * kBT, fb);
+          tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * kBK, nb * kRows, fb);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, kBT);
+      int stage = 0, aslot = 0;
+      uint32_t phase = 0, aphase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t use = (it >> 1) & 1;
+        if (!wait_t(bar_acc_empty + 8 * buf, use ^ 1, abort_flag, B200_DEVICE_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t d_addr = tmem_base + uint32_t(buf * C::kAccCols);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_t(bar_full + 8 * stage, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE) ||
+              !wait_t(bar_afull + 8 * aslot, aphase, abort_flag,
+                      B200_DEVICE_TIMEOUT_PIPELINE)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t x_addr = smem_u32(smem + stage * C::kStageBytes);
+          const uint32_t a_addr = tmem_base + uint32_t(C::kACol0 + aslot * C::kACols);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            mma_bf16_ta(d_addr, a_addr + uint32_t(kk * 8), desc_sw128(x_addr + kk * 32), idesc,
+                        (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar_empty + 8 * stage);
+          mma_commit(bar_aempty + 8 * aslot);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++aslot == C::kAStages) {
+            aslot = 0;
+            aphase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(bar_acc_full + 8 * buf);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const bool pairs_ok = (ldc % 2 == 0) && (n % 2 == 0) &&
+                          ((reinterpret_cast<uintptr_t>(out) & 3u) == 0);
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int mb = tile % num_m;
+      const int nb = tile / num_m;
+      const int buf = it & 1;
+      const uint32_t use = (it >> 1) & 1;
+      const bool acc_ok =
+          wait_t(bar_acc_full + 8 * buf, use, abort_flag, B200_DEVICE_TIMEOUT_ACCUM);
+      if (!__all_sync(0xffffffffu, acc_ok)) break;
+      tc_fence_after();
+      const int feat = nb * kRows + q * 32 + lane;  // this thread's output feature
+      const float bv = (bias != nullptr && feat < n) ? __bfloat162float(bias[feat]) : 0.0f;
+      const bool odd = (lane & 1) != 0;
+      const bool feat_pair_ok = feat - (odd ? 1 : 0) < n;
+      // 16 columns (tokens) per tcgen05.ld: few live registers.
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBT; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * C::kAccCols + c0), r);
+        const int tok0 = mb * kBT + c0;
+        if (pairs_ok) {
+          bf16* rowp = out + size_t(tok0 + (odd ? 1 : 0)) * ldc + (feat - (odd ? 1 : 0));
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float v0 = __uint_as_float(r[j]) + bv;      // token tok0 + j
+            const float v1 = __uint_as_float(r[j + 1]) + bv;  // token tok0 + j + 1
+            // even lane keeps token j and takes its odd neighbour's token j;
+            // odd lane keeps token j+1 and takes its even neighbour's j+1.
+            const float got = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+            const bf162 h = odd ? __floats2bfloat162_rn(got, v1) : __floats2bfloat162_rn(v0, got);
+            const int tok = tok0 + j + (odd ? 1 : 0);
+            if (tok < m && feat_pair_ok) {
+              *reinterpret_cast<bf162*>(rowp + size_t(j) * ldc) = h;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tok = tok0 + j;
+            if (tok < m && feat < n) {
+              out[size_t(tok) * ldc + feat] = __float2bfloat16_rn(__uint_as_float(r[j]) + bv);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_acc_empty + 8 * buf);
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------- dequantiser
+    // kGroups groups of four warps (one per TMEM lane quarter) take the
+    // k-block steps round-robin, so the latency chain of one step (wait,
+    // shared load, convert, tcgen05.st, wait::st, arrive) of a group overlaps
+    // the other groups' steps.  Step i = the i-th (tile, k-block) of this CTA.
+    const int dw = warp - 8;
+    const int quarter = dw & 3;
+    const int group = dw >> 2;
+    const int rl = quarter * 32 + lane;  // row of the tile = TMEM lane
+    const uint32_t t_lane = uint32_t(quarter * 32) << 16;
+    const int sw = (rl >> 1) & 3;        // 64-byte swizzle: chunk c -> c ^ sw
+    int tile = blockIdx.x, kb = group;
+    while (kb >= num_kb && tile < num_tiles) {
+      kb -= num_kb;
+      tile += gridDim.x;
+    }
+    // This thread's scale row for `tile` (recomputed when the tile changes).
+    int srow_tile = -1;
+    const uint16_t* srow = scales;
+    bool srow_ok = false;
+    for (int i = group; tile < num_tiles; i += kGroups) {
+      if (tile != srow_tile) {
+        srow_tile = tile;
+        const int row = (tile / num_m) * kRows + rl;
+        srow_ok = row < n;
+        srow = scales + size_t(srow_ok ? row : 0) * groups;
+      }
+      const uint32_t sv = srow_ok ? srow[kb] : 0u;
+      const int stage = i % C::kStages;
+      const uint32_t phase = uint32_t(i / C::kStages) & 1u;
+      const int aslot = i % C::kAStages;
+      const uint32_t aphase = uint32_t(i / C::kAStages) & 1u;
+      if (!wait_t(bar_full + 8 * stage, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) break;
+      const unsigned char* qt = smem + stage * C::kStageBytes + C::kXBytes + rl * kBK;
+      uint4 c[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[j] = *reinterpret_cast<const uint4*>(qt + ((j ^ sw) << 4));
+      const uint32_t s2bits = sv | (sv << 16);
+      const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
+      uint32_t v[32];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dq4(c[j].x, s2, v + 8 * j + 0);
+        dq4(c[j].y, s2, v + 8 * j + 2);
+        dq4(c[j].z, s2, v + 8 * j + 4);
+        dq4(c[j].w, s2, v + 8 * j + 6);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * stage);  // INT8 tile consumed
+      if (!wait_t(bar_aempty + 8 * aslot, aphase ^ 1, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE))
+        break;
+      tc_fence_after();
+      const uint32_t ta = tmem_base + t_lane + uint32_t(C::kACol0 + aslot * C::kACols);
+      tmem_st16(ta, v);
+      tmem_st16(ta + 16, v + 16);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_afull + 8 * aslot);
+      kb += kGroups;
+      while (kb >= num_kb && tile < num_tiles) {
+        kb -= num_kb;
+        tile += gridDim.x;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(512)
+                 : "memory");
+  }
+}
+
+template <int kBT, int kGroups>
+cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
+                      const bf16* input, bf16* output, int m, int n, int k, int ldc,
+                      cudaStream_t stream) {
+  using C = CfgT<kBT, kGroups>;
+  CUtensorMap tx, tq;
+  if (!encode_tmap_2d(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, kBT,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, kRows,
+                      CU_TENSOR_MAP_SWIZZLE_64B)) {
+    return cudaErrorInvalidValue;
+  }
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? 1ull << dev : 0ull;
+  if (bit == 0 || (attr_done.load(std::memory_order_acquire) & bit) == 0) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        gemm_w8t_kernel<kBT, kGroups>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(bit, std::memory_order_release);
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((m + kBT - 1) / kBT) * ((n + kRows - 1) / kRows);
+  const int grid = tiles < sms ? tiles : sms;
+  gemm_w8t_kernel<kBT, kGroups><<<grid, C::kThreads, C::kSmemBytes, stream>>>(
+      tx, tq, reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k, ldc);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_w8t_supported(const void* weight, const void* input, const void* output, int m,
+                        int n, int k) {
+  return m > 0 && n > 0 && k > 0 && k % 16 == 0 &&
+         (reinterpret_cast<uintptr_t>(weight) & 15u) == 0 &&
+         (reinterpret_cast<uintptr_t>(input) & 15u) == 0 && output != nullptr;
+}
+
+cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* bias,
+                            const bf16* input, bf16* output, int m, int n, int k, int ldc,
+                            cudaStream_t stream) {
+  static const int forced = [] {
+    const char* e = getenv("B200_W8T_TOKENS");
+    return e ? atoi(e) : 0;
+  }();
+  static const int groups = [] {
+    const char* e = getenv("B200_W8T_GROUPS");
+    return e ? atoi(e) : 4;
+  }();
+  if (forced == 128) {
+    return groups == 2 ? launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream)
+                       : launch_bt<128, 4>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  }
+  if (forced == 224) {
+    return launch_bt<224, 4>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  }
+  return groups == 2 ? launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream)
+                     : launch_bt<192, 4>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+}
+
+}  // namespace b200

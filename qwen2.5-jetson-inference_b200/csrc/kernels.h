@@ -73,6 +73,14 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream);
 
+// gemm_w8t.cu: W8A16 GEMM with the dequantised weight tiles in TMEM
+// (computes Y^T = W . X^T; any m, n; k % 16 == 0, 16-byte aligned W and X).
+bool gemm_w8t_supported(const void* weight, const void* input, const void* output, int m,
+                        int n, int k);
+cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* bias,
+                            const bf16* input, bf16* output, int m, int n, int k, int ldc,
+                            cudaStream_t stream);
+
 // Allocates (once per device) the BF16 weight buffer of the two-pass W8A16
 // prefill path; bytes == 0 means the default cap.
 cudaError_t reserve_gemm_scratch(size_t bytes);
