@@ -7,9 +7,9 @@
  * pointers, sizes and a CUDA stream; nothing here synchronises the stream
  * or keeps state between calls, except the device-side error word read by
  * b200_device_status, the fixed scratch array of b200_lm_head_bf16_noalloc,
- * and the BF16 weight buffer of the two-pass W8A16 prefill (allocated once
- * per device by b200_gemm_reserve_scratch or by the first large W8A16 GEMM;
- * no other call allocates device memory).  All work is enqueued
+ * the summation-order switch, and the BF16 weight buffer of the two-pass
+ * W8A16 prefill (allocated only by an explicit b200_gemm_reserve_scratch; no
+ * Linear call allocates device memory).  All work is enqueued
  * asynchronously on `stream`, exactly like the reference functions.
  *
  * Layouts (reference conventions, src/qwen2.cpp:231-330):
@@ -127,13 +127,14 @@ int b200_gemm_w8a16(const int8_t* weight, const uint16_t* scales,
                     int out_features, int in_features, b200_stream_t stream);
 
 /* Allocates now, on the current device, the BF16 weight buffer (at most
- * 256 MiB, or `bytes` if smaller and non-zero) that b200_gemm_w8a16 uses for
- * prefills of >= 1024 tokens: the INT8 weights are dequantised once to
- * bf16(q*s) and the tensor-core BF16 GEMM runs on them (same results as the
- * one-pass kernel).  Without this call the buffer is allocated by the first
- * such GEMM that is not being captured into a CUDA graph; while it is absent
- * the one-pass kernel runs.  Call it before capturing graphs.  The buffer
- * is one per device and shared: two such GEMMs running at the same time on
+ * 256 MiB, or `bytes` if smaller and non-zero) that b200_gemm_w8a16 may use
+ * for prefills of >= 1024 tokens, and of <= 128 tokens through a K >= 2048:
+ * the INT8 weights are dequantised once to bf16(q*s) and the tensor-core
+ * BF16 GEMM runs on them (same results as the one-pass kernels).  A GEMM call
+ * never allocates: without this reservation the one-pass kernels run (for
+ * >= 1024 tokens the one that keeps the dequantised weights in tensor
+ * memory).  Call it at start-up, outside stream capture.  The buffer is one
+ * per device and shared: two such GEMMs running at the same time on
  * different streams would race on it, so keep large W8A16 GEMMs of a device
  * in stream order (the reference engine uses one stream).  No reference
  * counterpart (the reference allocates its prefill workspace at start-up,

@@ -60,6 +60,11 @@ std::string json_list(const std::vector<T>& v) {
 
 }  // namespace
 
+// Present when the binary links libb200linear.so (e2e_b200), absent in
+// e2e_reference: the W8A16 prefill's BF16 weight buffer is reserved once at
+// start-up, as the reference engine allocates its own workspaces at load.
+extern "C" int b200_gemm_reserve_scratch(size_t bytes) __attribute__((weak));
+
 int main(int argc, char** argv) {
   try {
     infer::RuntimeOptions opt;
@@ -82,6 +87,10 @@ int main(int argc, char** argv) {
     if (prompt.empty()) throw infer::Error("--token-ids is required");
 
     infer::Qwen2Model model(arg(argc, argv, "--model"), opt);
+    if (b200_gemm_reserve_scratch != nullptr && opt.backend == infer::Device::kCuda &&
+        opt.precision == infer::Precision::kW8A16) {
+      if (b200_gemm_reserve_scratch(0) != 0) throw infer::Error("b200_gemm_reserve_scratch");
+    }
     if (!logits_out.empty()) {
       model.reset();
       model.prefill(prompt);

@@ -404,6 +404,12 @@ int b200_engine_create(b200_engine_t* out, const b200_engine_config* cfg,
       c.max_seq > 8192) {
     return B200_ERR_TOO_LARGE;
   }
+  // W8A16 prefill GEMMs dequantise the weights once into a library buffer:
+  // reserved here, with the engine's own buffers (GEMM calls never allocate).
+  if (c.w8 != 0) {
+    const cudaError_t re = b200::reserve_gemm_scratch(0);
+    if (re != cudaSuccess) return int(re);
+  }
   auto* e = new (std::nothrow) b200_engine;
   if (e == nullptr) return B200_ERR_INVALID_ARGUMENT;
   e->cfg = c;

@@ -1208,9 +1208,9 @@ bool gemm_tc_supported(bool w8, const void* weight, const void* input,
 // cores limits the one-pass kernel to about half the BF16 rate.  The BF16
 // weights go to a device buffer owned by the library (one per device,
 // kScratchCap bytes at most; W is processed in row blocks that fit).  The
-// buffer is allocated by b200_gemm_reserve_scratch, or by the first such GEMM
-// on a device that is not being captured into a CUDA graph; when it is not
-// available the one-pass kernel runs instead (same results).
+// buffer exists only after an explicit b200_gemm_reserve_scratch on that
+// device (a GEMM call never allocates); without it the one-pass kernels run
+// (same results).
 namespace {
 
 constexpr size_t kScratchCap = size_t(256) << 20;
@@ -1317,8 +1317,8 @@ cudaError_t gemm_w8_two_pass(const void* weight, const bf16* scales, const bf16*
 
 }  // namespace
 
-// W8A16 prefill through the TMEM-resident dequantised weights
-// (gemm_w8t.cu); B200_GEMM_W8T=1 selects it.
+// B200_GEMM_W8T=1 selects the TMEM-weight W8A16 kernel for every prompt
+// length (tuning / tests).
 bool use_w8t() {
   static const bool on = [] {
     const char* e = getenv("B200_GEMM_W8T");
@@ -1336,23 +1336,24 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
-  if (w8 && peers.n == 0 && use_w8t() && gemm_w8t_supported(weight, input, output, m, n, k)) {
-    return launch_gemm_w8t(weight, scales, bias, input, output, m, n, k, ldc, stream);
-  }
   if (w8 && (m >= kTwoPassMinTokens ||
              (m <= kTwoPassMaxFewTokens && k >= kTwoPassFewTokensMinK)) &&
       !getenv("B200_GEMM_ONE_PASS")) {
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    cudaStreamIsCapturing(stream, &cap);
+    // Only a buffer reserved beforehand (b200_gemm_reserve_scratch) is used;
+    // one too small for a 256-row block of this K leaves the one-pass path.
     Scratch sc;
-    // The buffer is allocated at its full cap (not this call's size) so that
-    // a later, larger GEMM can still use it; a buffer too small for one
-    // 256-row block of this K falls back to the one-pass kernel.
-    if (scratch_get(kScratchCap, cap == cudaStreamCaptureStatusNone, &sc) == cudaSuccess &&
+    if (scratch_get(kScratchCap, false, &sc) == cudaSuccess &&
         sc.bytes / (size_t(k) * 2) >= 256) {
       return gemm_w8_two_pass(weight, scales, bias, input, output, m, n, k, ldc, peers, sc,
                               stream);
     }
+  }
+  // One pass with the dequantised weights in TMEM for long prompts
+  // (gemm_w8t.cu); its epilogue has no peer stores, so the sharded form keeps
+  // the shared-memory dequant kernels.
+  if (w8 && peers.n == 0 && (m >= kTwoPassMinTokens || use_w8t()) &&
+      gemm_w8t_supported(weight, input, output, m, n, k)) {
+    return launch_gemm_w8t(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }
   const Tile t = choose_tile(w8, m, n);
   return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, ldc, peers,

@@ -81,6 +81,9 @@ struct CfgT {
   static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
   static_assert(kBT % 16 == 0 && kBT >= 16 && kBT <= 256, "MMA N");
   static_assert(kAStages >= 2, "TMEM: room for at least two A slots");
+  // A dequant group meets a given stage / A slot only on its own steps, so a
+  // wait can never be two barrier phases ahead.
+  static_assert(kStages % kGroups == 0 && kAStages % kGroups == 0, "group / ring sizes");
   static_assert(kXBytes % 1024 == 0, "128B-swizzle atoms");
 };
 
@@ -208,8 +211,10 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
         const uint32_t d_addr = tmem_base + uint32_t(buf * C::kAccCols);
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!wait_t(bar_full + 8 * stage, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE) ||
-              !wait_t(bar_afull + 8 * aslot, aphase, abort_flag,
+          // The dequant warps arrive on a_full only after they waited for
+          // this step's stage (X and INT8 land on the same barrier), so a_full
+          // also orders the X tile: one wait per k-block.
+          if (!wait_t(bar_afull + 8 * aslot, aphase, abort_flag,
                       B200_DEVICE_TIMEOUT_PIPELINE)) {
             ok = false;
             break;
@@ -417,19 +422,10 @@ cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* 
     const char* e = getenv("B200_W8T_TOKENS");
     return e ? atoi(e) : 0;
   }();
-  static const int groups = [] {
-    const char* e = getenv("B200_W8T_GROUPS");
-    return e ? atoi(e) : 4;
-  }();
   if (forced == 128) {
-    return groups == 2 ? launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream)
-                       : launch_bt<128, 4>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }
-  if (forced == 224) {
-    return launch_bt<224, 4>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-  }
-  return groups == 2 ? launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream)
-                     : launch_bt<192, 4>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  return launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
 }
 
 }  // namespace b200

@@ -805,12 +805,35 @@ struct BulkPlan {
   bool ref = false;  // reference summation order (kLPR 32, kR 1)
 };
 
+// SM count of the current device, looked up once per device (a host-side
+// cost paid on every GEMV call otherwise).
 int device_sm_count() {
+  static std::atomic<int> cached[64];
   int dev = 0;
   cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int count = 148;
   cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cached[dev].store(count, std::memory_order_relaxed);
   return count;
+}
+
+// Raises a kernel's dynamic shared-memory limit to the bulk budget once per
+// device (every plan stays below it).
+template <auto kKernel>
+cudaError_t bulk_smem_attr() {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(
+      kKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmemBudget + 8 * 1024);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
 }
 
 // Chooses the tile geometry (tiles of at least min_rows rows) by a simple
@@ -900,8 +923,8 @@ cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                         const GemvFusion& fusion) {
   auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef>
                          : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef>;
-  cudaError_t e = cudaFuncSetAttribute(
-      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
+  cudaError_t e = k == 896 ? bulk_smem_attr<gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef>>()
+                           : bulk_smem_attr<gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef>>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
