@@ -1064,7 +1064,7 @@ namespace {
 // launch so that callers with a fixed-size partials buffer can check the
 // grid first (b200_lm_head_bf16_noalloc).
 struct GemvPlan {
-  int kind = 0;  // 0: nothing to do, 1: generic, 2: TMA bulk, 3: stream
+  int kind = 0;  // 0: nothing to do, 1: generic, 2: TMA bulk, 3: stream, 4: i8 MMA
   BulkPlan bulk;
   GemvConfig cfg{0, 0};
   int grid = 0;
@@ -1082,10 +1082,23 @@ bool reference_fast_shape(bool w8, const void* weight, const void* input, int k,
   return lm_head ? k % 8 == 0 && k > 0 : k >= 8 && k % 8 == 0;
 }
 
+// The integer-tensor-core W8A16 GEMV (gemv_i8tc.cu): B200_GEMV_I8TC=1
+// selects it (read at every call).
+bool use_i8tc() {
+  const char* e = getenv("B200_GEMV_I8TC");
+  return e != nullptr && strcmp(e, "1") == 0;
+}
+
 GemvPlan plan_gemv(bool w8, const void* weight, const bf16* scales, int n,
                    int k, const void* input, bool lm_head, bool fused = false) {
   GemvPlan plan;
   if (n <= 0) return plan;
+  if (w8 && !fused && summation_order() == B200_ORDER_FAST && use_i8tc() &&
+      gemv_i8tc_supported(weight, input, scales, n, k)) {
+    plan.kind = 4;
+    plan.grid = gemv_i8tc_grid(n);
+    return plan;
+  }
   if (!fused && summation_order() == B200_ORDER_REFERENCE &&
       reference_fast_shape(w8, weight, input, k, lm_head) && n % 8 == 0 &&
       (!w8 || aligned16(scales)) && k <= 32768) {
@@ -1171,6 +1184,10 @@ cudaError_t launch_gemv(bool w8, const void* weight, const bf16* scales,
               : launch_generic<false>(weight, scales, bias, input, output, n,
                                       k, block_value, block_index, stream,
                                       nullptr);
+  }
+  if (plan.kind == 4) {
+    return launch_gemv_i8tc(weight, scales, bias, input, output, n, k, block_value,
+                            block_index, stream, nullptr);
   }
   if (plan.kind == 2) {
     const BulkPlan& p = plan.bulk;

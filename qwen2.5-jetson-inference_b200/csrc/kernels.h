@@ -48,6 +48,15 @@ cudaError_t launch_argmax_partials(const float* block_value,
 cudaError_t launch_argmax_bf16(const bf16* values, int n, int* out,
                                cudaStream_t stream);
 
+// gemv_i8tc.cu: W8A16 GEMV on the integer tensor cores (k % 64 == 0,
+// 64 <= k <= 6144, 16-byte aligned weight and input).
+bool gemv_i8tc_supported(const void* weight, const void* input, const void* scales, int n,
+                         int k);
+int gemv_i8tc_grid(int n);
+cudaError_t launch_gemv_i8tc(const void* weight, const bf16* scales, const bf16* bias,
+                             const bf16* input, bf16* output, int n, int k, float* block_value,
+                             int* block_index, cudaStream_t stream, int* grid_out);
+
 // gemm_simt.cu: any shape / alignment, CUDA cores.
 cudaError_t launch_gemm_simt(bool w8, const void* weight, const bf16* scales,
                              const bf16* bias, const bf16* input, bf16* output,
