@@ -68,14 +68,14 @@ namespace {
 constexpr int kTileRows = 128;
 constexpr int kKB = 128;          // K per stage (two quantisation groups)
 constexpr int kStageBytes = kTileRows * kKB;   // 16 KB
-constexpr int kStages = 6;
+constexpr int kMaxStages = 6;   // ring depth (measured: 12 stages ran slower)
 constexpr int kLimbRows = 16;     // MMA N (limbs 0..2 used)
 constexpr int kLimbBlock = kLimbRows * kKB;    // 2 KB per k-block
 constexpr int kChunkGroups = 8;   // groups handed to the epilogue at once
 constexpr int kChunkCols = kChunkGroups * 16;  // a group's D = 16 columns
 constexpr int kChunks = 4;        // TMEM chunk buffers (4 x 128 = 512 columns)
 constexpr int kThreads = 256;
-constexpr int kMaxK = 6144;      // limb tile + ring within shared memory
+constexpr int kMaxK = 5120;      // limb tile + scale tiles + ring within shared memory
 constexpr int kMinRows = 4 * 148 * kTileRows;
 
 // Instruction descriptor, kind::i8: D = S32, A = B = S8, both K-major.
@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __restrict__ scales,
                  const bf16* __restrict__ bias, const bf16* __restrict__ input,
                  bf16* __restrict__ output, int n_rows, int k, float* __restrict__ block_value,
-                 int* __restrict__ block_index) {
+                 int* __restrict__ block_index, const int kStages) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -117,14 +117,20 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
   const int groups = k / 64;
   unsigned char* ring = smem;
   unsigned char* limbs = ring + kStages * kStageBytes;             // num_kb x 2 KB
-  float* gfac = reinterpret_cast<float*>(limbs + num_kb * kLimbBlock);  // [groups]
+  // Two tiles' scales [128 rows x groups] BF16, each one contiguous range of
+  // the scale array (rows of a tile are consecutive).
+  const int stile_bytes = kTileRows * groups * 2;
+  unsigned char* stiles = limbs + num_kb * kLimbBlock;
+  float* gfac = reinterpret_cast<float*>(stiles + 2 * stile_bytes);  // [groups]
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(gfac + groups) + 15) & ~uintptr_t(15));
   const uint32_t bar_full = smem_u32(bars);
-  const uint32_t bar_empty = bar_full + 8 * kStages;
-  const uint32_t bar_dfull = bar_empty + 8 * kStages;
+  const uint32_t bar_empty = bar_full + 8 * kMaxStages;
+  const uint32_t bar_dfull = bar_empty + 8 * kMaxStages;
   const uint32_t bar_dempty = bar_dfull + 8 * kChunks;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2 * kChunks);
+  const uint32_t bar_sfull = bar_dempty + 8 * kChunks;
+  const uint32_t bar_sempty = bar_sfull + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 2 * kChunks + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* red_v = reinterpret_cast<float*>(tmem_slot + 2);
   int* red_i = reinterpret_cast<int*>(red_v + 4);
@@ -142,6 +148,10 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
     for (int d = 0; d < kChunks; ++d) {
       mbar_init(bar_dfull + 8 * d, 1);
       mbar_init(bar_dempty + 8 * d, 4);  // one arrival per epilogue warp
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_sfull + 8 * b, 1);
+      mbar_init(bar_sempty + 8 * b, 4);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -162,18 +172,37 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
   // requested before griddepcontrol.wait.
   const int total_steps = ((num_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) *
                           num_kb;
-  const int first = total_steps < kStages ? total_steps : kStages;
-  if (warp == 0 && lane == 0) {
-    int tile = blockIdx.x, kb = 0;
-    for (int i = 0; i < first; ++i) {
-      mbar_arrive_expect_tx(bar_full + 8 * i, kStageBytes);
-      tma_load_2d(smem_u32(ring + i * kStageBytes), &tmap_w, kb * kKB, tile * kTileRows,
-                  bar_full + 8 * i);
-      if (++kb == num_kb) {
-        kb = 0;
-        tile += gridDim.x;
-      }
+  // Steps issued before griddepcontrol.wait: none of them may wait (the
+  // consumers have not started), so at most one ring's worth and at most the
+  // two tiles whose scale buffers are free.
+  int first = total_steps < kStages ? total_steps : kStages;
+  if (first > 2 * num_kb) first = 2 * num_kb;
+  // Step i = k-block i % num_kb of this CTA's tile i / num_kb.  A tile's
+  // first step also brings its scales (bulk copy into buffer (i/num_kb) & 1).
+  auto issue = [&](int i) -> bool {
+    const int ti = i / num_kb, kb = i % num_kb;
+    const int tile = int(blockIdx.x) + ti * int(gridDim.x);
+    const int s = i % kStages;
+    if (i >= kStages && !wait_i(bar_empty + 8 * s, uint32_t(i / kStages - 1) & 1u, abort_flag))
+      return false;
+    if (kb == 0) {
+      const int b = ti & 1;
+      if (ti >= 2 && !wait_i(bar_sempty + 8 * b, uint32_t(ti / 2 - 1) & 1u, abort_flag))
+        return false;
+      const int rows = n_rows - tile * kTileRows < kTileRows ? n_rows - tile * kTileRows
+                                                            : kTileRows;
+      const uint32_t bytes = uint32_t(rows * groups * 2);
+      mbar_arrive_expect_tx(bar_sfull + 8 * b, bytes);
+      bulk_load(smem_u32(stiles + b * stile_bytes), scales + size_t(tile) * kTileRows * groups,
+                bytes, bar_sfull + 8 * b);
     }
+    mbar_arrive_expect_tx(bar_full + 8 * s, kStageBytes);
+    tma_load_2d(smem_u32(ring + s * kStageBytes), &tmap_w, kb * kKB, tile * kTileRows,
+                bar_full + 8 * s);
+    return true;
+  };
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < first; ++i) issue(i);
   }
 
   // ---- x as integer limbs (all threads), after the producing kernel.
@@ -223,24 +252,8 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int tile = blockIdx.x, kb = 0;
-      for (int i = 0; i < first; ++i) {
-        if (++kb == num_kb) {
-          kb = 0;
-          tile += gridDim.x;
-        }
-      }
       for (int i = first; i < total_steps; ++i) {
-        const int s = i % kStages;
-        const uint32_t ph = uint32_t(i / kStages - 1) & 1u;
-        if (!wait_i(bar_empty + 8 * s, ph, abort_flag)) break;
-        mbar_arrive_expect_tx(bar_full + 8 * s, kStageBytes);
-        tma_load_2d(smem_u32(ring + s * kStageBytes), &tmap_w, kb * kKB, tile * kTileRows,
-                    bar_full + 8 * s);
-        if (++kb == num_kb) {
-          kb = 0;
-          tile += gridDim.x;
-        }
+        if (!issue(i)) break;
       }
     }
   } else if (warp == 1) {
@@ -285,11 +298,17 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
     const int q = warp & 3;
     float best = -FLT_MAX;
     int best_index = INT_MAX;
-    int cc = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    int cc = 0, ti = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++ti) {
       const int row = tile * kTileRows + q * 32 + lane;
       const bool valid = row < n_rows;
-      const uint16_t* srow = scales + size_t(valid ? row : 0) * groups;
+      const int sb = ti & 1;
+      if (!__all_sync(0xffffffffu,
+                      wait_i(bar_sfull + 8 * sb, uint32_t(ti / 2) & 1u, abort_flag))) {
+        break;
+      }
+      const uint16_t* srow = reinterpret_cast<const uint16_t*>(stiles + sb * stile_bytes) +
+                             (q * 32 + lane) * groups;
       float acc = 0.0f;
       bool ok = true;
       for (int g0 = 0; g0 < groups; g0 += kChunkGroups, ++cc) {
@@ -328,6 +347,8 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sempty + 8 * sb);  // scales of this tile read
       if (!ok) break;
       if (valid) {
         const float b = bias ? __bfloat162float(bias[row]) : 0.0f;
@@ -369,11 +390,17 @@ gemv_i8tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __r
   }
 }
 
-int smem_bytes(int k) {
+int fixed_smem_bytes(int k) {
   const int num_kb = (k + kKB - 1) / kKB;
-  return 1024 + kStages * kStageBytes + num_kb * kLimbBlock + (k / 64) * 4 + 16 +
-         8 * (2 * kStages + 2 * kChunks) + 64;
+  return 1024 + num_kb * kLimbBlock + 2 * kTileRows * (k / 64) * 2 + (k / 64) * 4 + 16 +
+         8 * (2 * kMaxStages + 2 * kChunks + 4) + 64;
 }
+constexpr int kSmemLimit = 227 * 1024;
+int stages_for(int k) {
+  const int st = (kSmemLimit - fixed_smem_bytes(k)) / kStageBytes;
+  return st > kMaxStages ? kMaxStages : st;
+}
+int smem_bytes(int k) { return fixed_smem_bytes(k) + stages_for(k) * kStageBytes; }
 
 }  // namespace
 
@@ -381,9 +408,11 @@ bool gemv_i8tc_supported(const void* weight, const void* input, const void* scal
                          int k) {
   // Each 128-row tile walks its K serially: the kernel pays off only when
   // there are enough tiles for every SM several times over.
-  return n >= kMinRows && k >= 64 && k % 64 == 0 && k <= kMaxK &&
+  // Tile scale copies: 16-byte aligned, sizes a multiple of 16 (n % 8).
+  return stages_for(k) >= 4 && n >= kMinRows && n % 8 == 0 && k >= 64 && k % 64 == 0 && k <= kMaxK &&
          (reinterpret_cast<uintptr_t>(weight) & 15u) == 0 &&
-         (reinterpret_cast<uintptr_t>(input) & 15u) == 0 && scales != nullptr;
+         (reinterpret_cast<uintptr_t>(input) & 15u) == 0 && scales != nullptr &&
+         (reinterpret_cast<uintptr_t>(scales) & 15u) == 0;
 }
 
 int gemv_i8tc_grid(int n) {
@@ -415,7 +444,7 @@ cudaError_t launch_gemv_i8tc(const void* weight, const bf16* scales, const bf16*
   const unsigned long long bit = (dev >= 0 && dev < 64) ? 1ull << dev : 0ull;
   if (bit == 0 || (attr_done.load(std::memory_order_acquire) & bit) == 0) {
     const cudaError_t e = cudaFuncSetAttribute(
-        gemv_i8tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(kMaxK));
+        gemv_i8tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_release);
   }
@@ -433,7 +462,7 @@ cudaError_t launch_gemv_i8tc(const void* weight, const bf16* scales, const bf16*
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, gemv_i8tc_kernel, tw,
                             reinterpret_cast<const uint16_t*>(scales), bias, input, output, n, k,
-                            block_value, block_index);
+                            block_value, block_index, stages_for(k));
 }
 
 }  // namespace b200
