@@ -63,28 +63,30 @@ namespace {
 
 constexpr int kRows = 128;   // weight rows (output features) per tile
 constexpr int kBK = 64;      // K per k-block = one quantisation group
-template <int kBT, int kGroups>
+// kSub: quantisation groups (64 K values) per pipeline stage, 1 or 2.  The
+// MMA issuer pays a fixed ~300-500 cycles per barrier wait (measured), so a
+// stage must carry enough MMA work to keep the tensor pipe busy meanwhile.
+template <int kBT, int kSub>
 struct CfgT {
-  static constexpr int kDqWarps = 4 * kGroups;            // one per lane quarter
-
-  static constexpr int kXBytes = kBT * kBK * 2;           // tokens x 64 BF16
-  static constexpr int kQBytes = kRows * kBK;             // 128 x 64 INT8
+  static constexpr int kKS = kBK * kSub;                  // K per stage
+  static constexpr int kDqWarps = 8;                      // 2 per lane quarter
+  static constexpr int kXSub = kBT * kBK * 2;             // one 64-wide X sub-tile
+  static constexpr int kXBytes = kSub * kXSub;
+  static constexpr int kQBytes = kRows * kKS;             // 128 x kKS INT8
   static constexpr int kStageBytes = kXBytes + kQBytes;
   static constexpr int kStages =
       (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
   static constexpr int kAccCols = kBT;
-  static constexpr int kACols = kBK / 2;                  // 32 columns / slot
+  static constexpr int kACols = kKS / 2;                  // BF16 pairs per slot
   static constexpr int kAStages =
       (512 - 2 * kAccCols) / kACols > 8 ? 8 : (512 - 2 * kAccCols) / kACols;
   static constexpr int kACol0 = 2 * kAccCols;
   static constexpr int kThreads = (8 + kDqWarps) * 32;
   static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+  static_assert(kSub == 1 || kSub == 2, "one or two groups per stage");
   static_assert(kBT % 16 == 0 && kBT >= 16 && kBT <= 256, "MMA N");
-  static_assert(kAStages >= 2, "TMEM: room for at least two A slots");
-  // A dequant group meets a given stage / A slot only on its own steps, so a
-  // wait can never be two barrier phases ahead.
-  static_assert(kStages % kGroups == 0 && kAStages % kGroups == 0, "group / ring sizes");
-  static_assert(kXBytes % 1024 == 0, "128B-swizzle atoms");
+  static_assert(kAStages >= 2 && kStages >= 2, "ring sizes");
+  static_assert(kXSub % 1024 == 0, "128B-swizzle atoms");
 };
 
 __device__ __forceinline__ bool wait_t(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -112,13 +114,13 @@ __device__ __forceinline__ void dq4(uint32_t word, bf162 s2, uint32_t* out) {
   out[1] = *reinterpret_cast<const uint32_t*>(&d23);
 }
 
-template <int kBT, int kGroups>
-__global__ void __launch_bounds__(CfgT<kBT, kGroups>::kThreads, 1)
+template <int kBT, int kSub>
+__global__ void __launch_bounds__(CfgT<kBT, kSub>::kThreads, 1)
 gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_q,
                 const uint16_t* __restrict__ scales, const bf16* __restrict__ bias,
                 bf16* __restrict__ out, int m, int n, int k, int ldc) {
-  using C = CfgT<kBT, kGroups>;
+  using C = CfgT<kBT, kSub>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -139,16 +141,16 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int num_m = (m + kBT - 1) / kBT;
   const int num_n = (n + kRows - 1) / kRows;
   const int num_tiles = num_m * num_n;
-  const int num_kb = (k + kBK - 1) / kBK;
+  const int num_kb = (k + C::kKS - 1) / C::kKS;
   const int groups = (k + 63) / 64;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, 1 + 4);  // MMA commit + one dequant group
+      mbar_init(bar_empty + 8 * s, 1 + C::kDqWarps);  // MMA commit + dequant warps
     }
     for (int a = 0; a < C::kAStages; ++a) {
-      mbar_init(bar_afull + 8 * a, 4);
+      mbar_init(bar_afull + 8 * a, C::kDqWarps);
       mbar_init(bar_aempty + 8 * a, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -185,8 +187,12 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
           unsigned char* st = smem + stage * C::kStageBytes;
           const uint32_t fb = bar_full + 8 * stage;
           mbar_arrive_expect_tx(fb, C::kStageBytes);
-          tma_load_2d(smem_u32(st), &tmap_x, kb * kBK, mb * kBT, fb);
-          tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * kBK, nb * kRows, fb);
+#pragma unroll
+          for (int sub = 0; sub < kSub; ++sub) {
+            tma_load_2d(smem_u32(st + sub * C::kXSub), &tmap_x, kb * C::kKS + sub * kBK,
+                        mb * kBT, fb);
+          }
+          tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS, nb * kRows, fb);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -223,8 +229,9 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
           const uint32_t x_addr = smem_u32(smem + stage * C::kStageBytes);
           const uint32_t a_addr = tmem_base + uint32_t(C::kACol0 + aslot * C::kACols);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            mma_bf16_ta(d_addr, a_addr + uint32_t(kk * 8), desc_sw128(x_addr + kk * 32), idesc,
+          for (int kk = 0; kk < C::kKS / 16; ++kk) {
+            mma_bf16_ta(d_addr, a_addr + uint32_t(kk * 8),
+                        desc_sw128(x_addr + (kk >> 2) * C::kXSub + (kk & 3) * 32), idesc,
                         (kb > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(bar_empty + 8 * stage);
@@ -297,68 +304,78 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
   } else if (warp >= 8) {
     // ---------------------------------------------------------- dequantiser
-    // kGroups groups of four warps (one per TMEM lane quarter) take the
-    // k-block steps round-robin, so the latency chain of one step (wait,
-    // shared load, convert, tcgen05.st, wait::st, arrive) of a group overlaps
-    // the other groups' steps.  Step i = the i-th (tile, k-block) of this CTA.
+    // Warps w and w+4 cover TMEM lane quarter w % 4 and split each stage's K
+    // range in two parts (part p: kKS/2 values = one group when kSub == 2).
     const int dw = warp - 8;
     const int quarter = dw & 3;
-    const int group = dw >> 2;
+    const int part = dw >> 2;
     const int rl = quarter * 32 + lane;  // row of the tile = TMEM lane
     const uint32_t t_lane = uint32_t(quarter * 32) << 16;
-    const int sw = (rl >> 1) & 3;        // 64-byte swizzle: chunk c -> c ^ sw
-    int tile = blockIdx.x, kb = group;
-    while (kb >= num_kb && tile < num_tiles) {
-      kb -= num_kb;
-      tile += gridDim.x;
-    }
-    // This thread's scale row for `tile` (recomputed when the tile changes).
-    int srow_tile = -1;
-    const uint16_t* srow = scales;
-    bool srow_ok = false;
-    for (int i = group; tile < num_tiles; i += kGroups) {
-      if (tile != srow_tile) {
-        srow_tile = tile;
-        const int row = (tile / num_m) * kRows + rl;
-        srow_ok = row < n;
-        srow = scales + size_t(srow_ok ? row : 0) * groups;
-      }
-      const uint32_t sv = srow_ok ? srow[kb] : 0u;
-      const int stage = i % C::kStages;
-      const uint32_t phase = uint32_t(i / C::kStages) & 1u;
-      const int aslot = i % C::kAStages;
-      const uint32_t aphase = uint32_t(i / C::kAStages) & 1u;
-      if (!wait_t(bar_full + 8 * stage, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) break;
-      const unsigned char* qt = smem + stage * C::kStageBytes + C::kXBytes + rl * kBK;
-      uint4 c[4];
+    // INT8 tile swizzle: 64-byte rows (kSub 1): chunk c at c ^ ((r >> 1) & 3);
+    // 128-byte rows (kSub 2): chunk c at c ^ (r & 7).
+    const int sw = kSub == 1 ? ((rl >> 1) & 3) : (rl & 7);
+    constexpr int kChunks = kSub * 2;  // 16-byte chunks per thread per stage
+    int stage = 0, aslot = 0;
+    uint32_t phase = 0, aphase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      const int row = (tile / num_m) * kRows + rl;
+      const bool srow_ok = row < n;
+      const uint16_t* srow = scales + size_t(srow_ok ? row : 0) * groups;
+      // group of this thread's part in k-block kb: kb * kSub + part (kSub 2)
+      // or kb (kSub 1)
+      auto group_of = [&](int kb) { return kSub == 2 ? kb * 2 + part : kb; };
+      uint32_t s_next = (srow_ok && group_of(0) < groups) ? srow[group_of(0)] : 0u;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const uint32_t sv = s_next;
+        if (kb + 1 < num_kb) {
+          const int g1 = group_of(kb + 1);
+          s_next = (srow_ok && g1 < groups) ? srow[g1] : 0u;
+        }
+        if (!wait_t(bar_full + 8 * stage, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) {
+          ok = false;
+          break;
+        }
+        const unsigned char* qt = smem + stage * C::kStageBytes + C::kXBytes + rl * C::kKS;
+        uint4 c[kChunks];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) c[j] = *reinterpret_cast<const uint4*>(qt + ((j ^ sw) << 4));
-      const uint32_t s2bits = sv | (sv << 16);
-      const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
-      uint32_t v[32];
+        for (int j = 0; j < kChunks; ++j) {
+          c[j] = *reinterpret_cast<const uint4*>(qt + (((part * kChunks + j) ^ sw) << 4));
+        }
+        const uint32_t s2bits = sv | (sv << 16);
+        const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
+        uint32_t v[8 * kChunks];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        dq4(c[j].x, s2, v + 8 * j + 0);
-        dq4(c[j].y, s2, v + 8 * j + 2);
-        dq4(c[j].z, s2, v + 8 * j + 4);
-        dq4(c[j].w, s2, v + 8 * j + 6);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_empty + 8 * stage);  // INT8 tile consumed
-      if (!wait_t(bar_aempty + 8 * aslot, aphase ^ 1, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE))
-        break;
-      tc_fence_after();
-      const uint32_t ta = tmem_base + t_lane + uint32_t(C::kACol0 + aslot * C::kACols);
-      tmem_st16(ta, v);
-      tmem_st16(ta + 16, v + 16);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_afull + 8 * aslot);
-      kb += kGroups;
-      while (kb >= num_kb && tile < num_tiles) {
-        kb -= num_kb;
-        tile += gridDim.x;
+        for (int j = 0; j < kChunks; ++j) {
+          dq4(c[j].x, s2, v + 8 * j + 0);
+          dq4(c[j].y, s2, v + 8 * j + 2);
+          dq4(c[j].z, s2, v + 8 * j + 4);
+          dq4(c[j].w, s2, v + 8 * j + 6);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_empty + 8 * stage);  // INT8 tile consumed
+        if (!wait_t(bar_aempty + 8 * aslot, aphase ^ 1, abort_flag,
+                    B200_DEVICE_TIMEOUT_PIPELINE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ta = tmem_base + t_lane +
+                            uint32_t(C::kACol0 + aslot * C::kACols + part * (C::kACols / 2));
+#pragma unroll
+        for (int j = 0; j < kChunks / 2; ++j) tmem_st16(ta + 16 * j, v + 16 * j);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_afull + 8 * aslot);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++aslot == C::kAStages) {
+          aslot = 0;
+          aphase ^= 1;
+        }
       }
     }
   }
@@ -374,16 +391,16 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
-template <int kBT, int kGroups>
+template <int kBT, int kSub>
 cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
                       const bf16* input, bf16* output, int m, int n, int k, int ldc,
                       cudaStream_t stream) {
-  using C = CfgT<kBT, kGroups>;
+  using C = CfgT<kBT, kSub>;
   CUtensorMap tx, tq;
   if (!encode_tmap_2d(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, kBT,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kBK, kRows,
-                      CU_TENSOR_MAP_SWIZZLE_64B)) {
+      !encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, C::kKS, kRows,
+                      kSub == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
   static std::atomic<unsigned long long> attr_done{0};
@@ -392,7 +409,7 @@ cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
   const unsigned long long bit = (dev >= 0 && dev < 64) ? 1ull << dev : 0ull;
   if (bit == 0 || (attr_done.load(std::memory_order_acquire) & bit) == 0) {
     const cudaError_t e = cudaFuncSetAttribute(
-        gemm_w8t_kernel<kBT, kGroups>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        gemm_w8t_kernel<kBT, kSub>, cudaFuncAttributeMaxDynamicSharedMemorySize,
         C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_release);
@@ -401,7 +418,7 @@ cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = ((m + kBT - 1) / kBT) * ((n + kRows - 1) / kRows);
   const int grid = tiles < sms ? tiles : sms;
-  gemm_w8t_kernel<kBT, kGroups><<<grid, C::kThreads, C::kSmemBytes, stream>>>(
+  gemm_w8t_kernel<kBT, kSub><<<grid, C::kThreads, C::kSmemBytes, stream>>>(
       tx, tq, reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k, ldc);
   return cudaGetLastError();
 }
@@ -418,12 +435,13 @@ bool gemm_w8t_supported(const void* weight, const void* input, const void* outpu
 cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* bias,
                             const bf16* input, bf16* output, int m, int n, int k, int ldc,
                             cudaStream_t stream) {
-  static const int forced = [] {
-    const char* e = getenv("B200_W8T_TOKENS");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced == 128) {
-    return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  // Tile shape: tokens per tile x quantisation groups per stage
+  // (B200_W8T_CFG=192x2 | 192x1 | 128x2 | 128x1 overrides, for tuning).
+  const char* cfg = getenv("B200_W8T_CFG");
+  if (cfg != nullptr) {
+    if (!strcmp(cfg, "192x1")) return launch_bt<192, 1>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "128x1")) return launch_bt<128, 1>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "128x2")) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }
   return launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
 }
