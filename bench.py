@@ -215,12 +215,15 @@ def per_shape(sweep, calls=200):
 
 def gemm_sweep(b200, device, reps=10):
     """M x five shapes x {W8A16, BF16}.  `us` / TFLOP/s: device
-    time per call, `reps` calls replayed from a CUDA graph (CUDA events);
-    `us_eager_python`: the same calls launched one by one from Python
-    (ctypes), host launch cost included."""
+    time per call, `reps` calls replayed from a CUDA graph (CUDA events).
+    `weights`: "w8a16" = the default W8A16 path (one pass: no call
+    allocates; M >= 1024 keeps the dequantised weights in tensor memory),
+    "bf16", and "w8a16_reserved" = W8A16 after b200_gemm_reserve_scratch
+    (dequantise once into the reserved buffer + BF16 GEMM) for the shapes
+    that route takes (M >= 1024 and M x N >= 2^25 outputs)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(99)
-    res = []
+    mats = []
     for (k, n) in SHAPES:
         w = torch.randn(n, k, generator=gen, device=device) * 0.02
         q, s = b200.quantize_groupwise(w)
@@ -228,34 +231,37 @@ def gemm_sweep(b200, device, reps=10):
         del w
         bias = (torch.randn(n, generator=gen, device=device) * 0.02).to(torch.bfloat16) \
             if (k, n) in BIAS_SHAPES else None
+        mats.append((k, n, q, s, wb, bias))
+
+    def time_one(label, k, n, q, s, wb, bias, m):
+        x = torch.randn(m, k, generator=gen, device=device).to(torch.bfloat16)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+
+        def run():
+            if label == "bf16":
+                b200.gemm_bf16(wb, bias, x, y, m, n, k)
+            else:
+                b200.gemm_w8a16(q, s, 64, bias, x, y, m, n, k)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        g = capture(lambda: [run() for _ in range(reps)])
+        t = time_graph(g, 3, 1) / reps
+        del g, x, y
+        return {"weights": label, "m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
+                "tflops": round(2.0 * m * n * k / t / 1e12, 1)}
+
+    res = []
+    for (k, n, q, s, wb, bias) in mats:
         for m in PREFILL_M:
-            x = torch.randn(m, k, generator=gen, device=device).to(torch.bfloat16)
-            y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
-            for w8 in (True, False):
-                def run():
-                    if w8:
-                        b200.gemm_w8a16(q, s, 64, bias, x, y, m, n, k)
-                    else:
-                        b200.gemm_bf16(wb, bias, x, y, m, n, k)
-                for _ in range(3):
-                    run()
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-                e0.record()
-                for _ in range(reps):
-                    run()
-                e1.record()
-                torch.cuda.synchronize()
-                t_eager = e0.elapsed_time(e1) / 1e3 / reps
-                # device time: `reps` back-to-back calls replayed from a graph
-                g = capture(lambda: [run() for _ in range(reps)])
-                t = time_graph(g, 3, 1) / reps
-                del g
-                res.append({"w8": w8, "m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
-                            "tflops": round(2.0 * m * n * k / t / 1e12, 1),
-                            "us_eager_python": round(t_eager * 1e6, 2)})
-            del x, y
-        del q, s, wb
+            res.append(time_one("w8a16", k, n, q, s, wb, bias, m))
+            res.append(time_one("bf16", k, n, q, s, wb, bias, m))
+    if b200.ABI.b200_gemm_reserve_scratch(0) == 0:
+        for (k, n, q, s, wb, bias) in mats:
+            for m in PREFILL_M:
+                if m >= 1024 and m * n >= 32 * 1024 * 1024:
+                    res.append(time_one("w8a16_reserved", k, n, q, s, wb, bias, m))
+    del mats
     torch.cuda.empty_cache()
     return res
 
@@ -306,6 +312,8 @@ def sharded_bench(b200, world, rank, device, reps=5):
     every shard, and the LM head's argmax against the unsharded kernel."""
     import importlib
     sh = importlib.import_module("qwen25_b200.sharded")
+    # a sharded deployment reserves the W8A16 prefill buffer at start-up
+    assert b200.ABI.b200_gemm_reserve_scratch(0) == 0
     comm = (sh.Comm.from_process_group() if world > 1
             else sh.Comm(sh.new_unique_id(), 1, 0))
     out = {"gemm": [], "lm_head": None}
@@ -824,19 +832,33 @@ def main():
     e2e = None
     if rank == 0 or world > 1:
         # ---- e2e: public API, pinned host x in, host y out, every step.
-        xs_host = [it["x"].cpu().pin_memory() for it in sweep.items]
-        ys_host = [torch.empty(it["n"], dtype=torch.bfloat16).pin_memory()
-                   for it in sweep.items]
-        xs_dev = [torch.empty_like(it["x"]) for it in sweep.items]
+        # The five inputs share one pinned host buffer and one device buffer
+        # (one copy in), the five outputs one device and one pinned host
+        # buffer (one copy out); the calls pass raw pointers and the stream
+        # handle, as a C or C++ caller of the ABI would.
+        ks = [it["k"] for it in sweep.items]
+        ns = [it["n"] for it in sweep.items]
+        x_host = torch.cat([it["x"].cpu() for it in sweep.items]).pin_memory()
+        x_dev = torch.empty_like(x_host, device=device)
+        y_dev = torch.empty(sum(ns), dtype=torch.bfloat16, device=device)
+        y_host = torch.empty(sum(ns), dtype=torch.bfloat16).pin_memory()
+        x_off = [sum(ks[:i]) for i in range(len(ks))]
+        y_off = [sum(ns[:i]) for i in range(len(ns))]
+        x_views = [x_dev[o:o + kk] for o, kk in zip(x_off, ks)]
+        y_views = [y_dev[o:o + nn] for o, nn in zip(y_off, ns)]
+        stream = torch.cuda.current_stream()
+        handle = stream.cuda_stream
         e2e_steps = max(1, args.steps)
-        h2d = sum(2 * it["k"] for it in sweep.items)
-        d2h = sum(2 * it["n"] for it in sweep.items)
+        h2d = x_host.numel() * 2
+        d2h = y_host.numel() * 2
 
         def e2e_step(step):
+            x_dev.copy_(x_host, non_blocking=True)
             for i, it in enumerate(sweep.items):
-                xs_dev[i].copy_(xs_host[i], non_blocking=True)
-                sweep.call(it, step, x=xs_dev[i])
-                ys_host[i].copy_(it["y"], non_blocking=True)
+                w, sc = it["copies"][step % len(it["copies"])]
+                b200.gemv_w8a16(w, sc, 64, it["bias"], x_views[i], y_views[i], it["n"],
+                                it["k"], handle)
+            y_host.copy_(y_dev, non_blocking=True)
         for s in range(2):
             e2e_step(s)
         torch.cuda.synchronize()
@@ -850,8 +872,9 @@ def main():
         e2e = {"value": round(e2e_bytes / e2e_s / 1e9, 2), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "note": "one pass of the 5-shape sweep per step through the Python "
-                       "API (ctypes -> C ABI), x copied from pinned host memory and y "
-                       "read back each step; host wall clock, max over ranks"}
+                       "API (ctypes -> C ABI), the five x copied from one pinned host "
+                       "buffer and the five y read back into one, every step; host "
+                       "wall clock, max over ranks"}
     del sweep
     torch.cuda.empty_cache()
 
@@ -898,7 +921,7 @@ def main():
             "sweep_w8a16": table(shapes_w8, ["k", "n", "us", "gbs"]),
             "sweep_bf16": table(shapes_bf16, ["k", "n", "us", "gbs"]),
             "gemm_sweep": None if gemm is None else table(
-                gemm, ["w8", "m", "k", "n", "us", "tflops"]),
+                gemm, ["weights", "m", "k", "n", "us", "tflops"]),
             # the end of the line survives in truncated logs: keep the
             # multi-GPU and end-to-end results last
             "e2e_decode": e2e_decode,

@@ -128,8 +128,8 @@ int b200_gemm_w8a16(const int8_t* weight, const uint16_t* scales,
 
 /* Allocates now, on the current device, the BF16 weight buffer (at most
  * 256 MiB, or `bytes` if smaller and non-zero) that b200_gemm_w8a16 may use
- * for prefills of >= 1024 tokens, and of <= 128 tokens through a K >= 2048:
- * the INT8 weights are dequantised once to bf16(q*s) and the tensor-core
+ * for large prefills (>= 1024 tokens and >= 2^25 outputs, where it measured
+ * faster): the INT8 weights are dequantised once to bf16(q*s) and the tensor-core
  * BF16 GEMM runs on them (same results as the one-pass kernels).  A GEMM call
  * never allocates: without this reservation the one-pass kernels run (for
  * >= 1024 tokens the one that keeps the dequantised weights in tensor

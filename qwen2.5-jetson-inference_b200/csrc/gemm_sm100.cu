@@ -1215,12 +1215,9 @@ namespace {
 
 constexpr size_t kScratchCap = size_t(256) << 20;
 constexpr int kTwoPassMinTokens = 1024;
-// Few tokens with a long K (a short prompt through down_proj): the one-pass
-// kernel's per-k-block dequant hand-off makes each tile's K walk slow and
-// there are few tiles; dequantising W once and running narrow BF16 tiles
-// is faster, with the same results.
-constexpr int kTwoPassMaxFewTokens = 128;
-constexpr int kTwoPassFewTokensMinK = 2048;
+// Measured: the extra pass over W pays off only for large outputs (e.g.
+// 8192 x 4864 or 2048 x 151936); below, the one-pass kernels are faster.
+constexpr double kTwoPassMinOutputs = 32.0 * 1024 * 1024;
 
 struct Scratch {
   void* ptr = nullptr;
@@ -1336,8 +1333,7 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
-  if (w8 && (m >= kTwoPassMinTokens ||
-             (m <= kTwoPassMaxFewTokens && k >= kTwoPassFewTokensMinK)) &&
+  if (w8 && m >= kTwoPassMinTokens && double(m) * double(n) >= kTwoPassMinOutputs &&
       !getenv("B200_GEMM_ONE_PASS")) {
     // Only a buffer reserved beforehand (b200_gemm_reserve_scratch) is used;
     // one too small for a 256-row block of this K leaves the one-pass path.

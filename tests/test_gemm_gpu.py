@@ -153,7 +153,7 @@ def test_gemm_output_guard_band_and_status(b200, oracle, cuda):
     assert b200.device_status() == 0
 
 
-@pytest.mark.parametrize("m,k,n", [(1024, 896, 4864), (2048, 896, 151936), (1100, 4864, 904)])
+@pytest.mark.parametrize("m,k,n", [(8192, 896, 4864), (2048, 896, 151936), (4100, 1088, 8200)])
 def test_w8a16_one_pass_and_two_pass_agree(b200, oracle, cuda, m, k, n):
     """Large-M W8A16 with a reserved buffer runs as dequantise-once + BF16
     tensor-core GEMM; the one-pass kernel that keeps the dequantised weights
