@@ -108,7 +108,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_w,
                const bf16* __restrict__ scales, const bf16* __restrict__ bias,
                bf16* __restrict__ out, int m, int n, int k, int ldc,
-               const PeerOuts peers, int a_rows) {
+               const PeerOuts peers, int a_rows, int kchunk,
+               float* __restrict__ partial) {
   using C = Cfg<kW8, kMSub, kBN>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -130,7 +131,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int num_m = (m + C::kBM - 1) / C::kBM;
   const int num_n = (n + kBN - 1) / kBN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = (k + kBK - 1) / kBK;
+  // K split (grid z): this CTA walks K values [k_begin, k_begin + kchunk) and,
+  // with `partial`, stores FP32 sums without bias into slab z of it.
+  const int k_begin = int(blockIdx.z) * kchunk;
+  const int k_len = k - k_begin < kchunk ? k - k_begin : kchunk;
+  const int num_kb = (k_len + kBK - 1) / kBK;
+  const int kb0 = k_begin / kBK;  // kchunk is a multiple of kBK
   const int groups = (k + 63) / 64;
 
   if (threadIdx.x == 0) {
@@ -159,6 +165,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel; X (and the output) are touched only after it has completed.
+  pdl_launch_dependents();
+  pdl_wait_primary();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -179,11 +189,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           mbar_arrive_expect_tx(fb, C::kTxBytes - kMSub * (128 - a_rows) * kBK * 2);
 #pragma unroll
           for (int s = 0; s < kMSub; ++s) {
-            tma_load_2d(smem_u32(st + s * C::kABytes), &tmap_x, kb * kBK,
+            tma_load_2d(smem_u32(st + s * C::kABytes), &tmap_x, (kb0 + kb) * kBK,
                         mb * C::kBM + s * 128, fb);
           }
           unsigned char* wdst = st + kMSub * C::kABytes + (kW8 ? C::kBBytes : 0);
-          tma_load_2d(smem_u32(wdst), &tmap_w, kb * kBK, nb * kBN, fb);
+          tma_load_2d(smem_u32(wdst), &tmap_w, (kb0 + kb) * kBK, nb * kBN, fb);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -263,7 +273,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         uint32_t(buf * C::kAccCols + s * kBN + c0),
                     r);
           const int col0 = nb * kBN + c0;
-          if (row < m && col0 < n) {
+          if (partial != nullptr) {
+            // K-split partial: FP32, no bias, slab blockIdx.z of [m][n]
+            if (row < m) {
+              float* pd = partial + (size_t(blockIdx.z) * m + row) * n + col0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col0 + j < n) pd[j] = __uint_as_float(r[j]);
+              }
+            }
+          } else if (row < m && col0 < n) {
             bf16* dst = out + size_t(row) * ldc + col0;
             if (vec_ok && col0 + 32 <= n) {
 #pragma unroll
@@ -330,7 +349,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         const int item = dt + p * (C::kDqWarps * 32);
         const int row = nb * kBN + (item >> 2);
         const uint32_t v =
-            (tile < num_tiles && row < n) ? sbits[size_t(row) * groups + kb] : 0u;
+            (tile < num_tiles && row < n) ? sbits[size_t(row) * groups + kb0 + kb] : 0u;
         out[p] = v | (v << 16);
       }
     };
@@ -616,6 +635,10 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_x,
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel; X (and the output) are touched only after it has completed.
+  pdl_launch_dependents();
+  pdl_wait_primary();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -1045,7 +1068,8 @@ int sm_count() {
 template <bool kW8, int kMSub, int kBN>
 cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
                        const bf16* input, bf16* output, int m, int n, int k,
-                       int ldc, const PeerOuts& peers, cudaStream_t stream) {
+                       int ldc, const PeerOuts& peers, cudaStream_t stream,
+                       int splits = 1, float* partial = nullptr) {
   using C = Cfg<kW8, kMSub, kBN>;
   CUtensorMap tx, tw;
   // A short prompt (m < 128, one 128-row sub-tile) loads only its rows.
@@ -1066,10 +1090,23 @@ cudaError_t launch_cfg(const void* weight, const bf16* scales, const bf16* bias,
   cudaError_t e = ensure_smem_attr<gemm_tc_kernel<kW8, kMSub, kBN>>(C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int tiles = ((m + C::kBM - 1) / C::kBM) * ((n + kBN - 1) / kBN);
-  const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, scales, bias,
-                                                        output, m, n, k, ldc, peers, a_rows);
-  return cudaGetLastError();
+  // K split over grid z: chunks of whole 64-wide k-blocks
+  const int kchunk = splits > 1 ? ((k + splits - 1) / splits + kBK - 1) / kBK * kBK : k;
+  const int zs = (k + kchunk - 1) / kchunk;
+  const int per_z = sm_count() / zs > 0 ? sm_count() / zs : 1;
+  const int grid = tiles < per_z ? tiles : per_z;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, zs);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k, ldc, peers,
+                            a_rows, kchunk, splits > 1 ? partial : nullptr);
 }
 
 template <bool kW8>
@@ -1101,13 +1138,15 @@ cudaError_t launch_pair(const void* weight, const bf16* scales, const bf16* bias
   cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, tx, tw, scales, bias, output, m, n, k, ldc, peers);
 }
 
@@ -1312,6 +1351,70 @@ cudaError_t gemm_w8_two_pass(const void* weight, const bf16* scales, const bf16*
   return cudaSuccess;
 }
 
+// Sum of the K-split partials in split order, + bias, BF16 RNE.
+__global__ void __launch_bounds__(256)
+splitk_reduce_kernel(const float* __restrict__ partial, int splits, const bf16* __restrict__ bias,
+                     bf16* __restrict__ out, int m, int n, int ldc) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const size_t total = size_t(m) * n;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const int row = int(i / n), col = int(i - size_t(row) * n);
+    float acc = partial[i];
+    for (int z = 1; z < splits; ++z) acc += partial[size_t(z) * total + i];
+    if (bias) acc += __bfloat162float(bias[col]);
+    out[size_t(row) * ldc + col] = __float2bfloat16_rn(acc);
+  }
+}
+
+// Short prompts in the fast summation order: the few output tiles each walk
+// K split over grid z (FP32 partials into the reserved buffer, reduced in a
+// fixed order).  Returns cudaErrorNotSupported when it does not apply.
+constexpr int kSplitMaxTokens = 128;
+cudaError_t gemm_split_k(bool w8, const void* weight, const bf16* scales, const bf16* bias,
+                         const bf16* input, bf16* output, int m, int n, int k, int ldc,
+                         cudaStream_t stream) {
+  if (m > kSplitMaxTokens || summation_order() != B200_ORDER_FAST ||
+      getenv("B200_GEMM_NO_SPLITK") != nullptr) {
+    return cudaErrorNotSupported;
+  }
+  const int bn = w8 ? 64 : 32;
+  const int tiles = (n + bn - 1) / bn;  // one 128-row tile covers the prompt
+  const int num_kb = (k + kBK - 1) / kBK;
+  int splits = sm_count() / tiles;
+  if (splits > num_kb) splits = num_kb;
+  if (splits > 16) splits = 16;
+  if (splits < 2) return cudaErrorNotSupported;
+  const int kchunk = ((k + splits - 1) / splits + kBK - 1) / kBK * kBK;
+  const int zs = (k + kchunk - 1) / kchunk;
+  Scratch sc;
+  if (scratch_get(kScratchCap, false, &sc) != cudaSuccess ||
+      sc.bytes < size_t(zs) * m * n * sizeof(float)) {
+    return cudaErrorNotSupported;
+  }
+  float* part = static_cast<float*>(sc.ptr);
+  cudaError_t e = w8 ? launch_cfg<true, 1, 64>(weight, scales, nullptr, input, output, m, n, k,
+                                               ldc, PeerOuts{}, stream, splits, part)
+                     : launch_cfg<false, 1, 32>(weight, scales, nullptr, input, output, m, n, k,
+                                                ldc, PeerOuts{}, stream, splits, part);
+  if (e != cudaSuccess) return e;
+  const size_t total = size_t(m) * n;
+  int grid = int((total + 255) / 256);
+  if (grid > 4 * sm_count()) grid = 4 * sm_count();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, (const float*)part, zs, bias, output, m,
+                            n, ldc);
+}
+
 }  // namespace
 
 // B200_GEMM_W8T=1 selects the TMEM-weight W8A16 kernel for every prompt
@@ -1333,6 +1436,11 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
+  if (peers.n == 0 && m <= kSplitMaxTokens) {
+    const cudaError_t e =
+        gemm_split_k(w8, weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (w8 && m >= kTwoPassMinTokens && double(m) * double(n) >= kTwoPassMinOutputs &&
       !getenv("B200_GEMM_ONE_PASS")) {
     // Only a buffer reserved beforehand (b200_gemm_reserve_scratch) is used;

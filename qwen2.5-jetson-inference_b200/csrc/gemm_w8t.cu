@@ -171,6 +171,10 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel; X (and the output) are touched only after it has completed.
+  pdl_launch_dependents();
+  pdl_wait_primary();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -418,9 +422,19 @@ cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = ((m + kBT - 1) / kBT) * ((n + kRows - 1) / kRows);
   const int grid = tiles < sms ? tiles : sms;
-  gemm_w8t_kernel<kBT, kSub><<<grid, C::kThreads, C::kSmemBytes, stream>>>(
-      tx, tq, reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k, ldc);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_w8t_kernel<kBT, kSub>, tx, tq,
+                            reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k,
+                            ldc);
 }
 
 }  // namespace

@@ -105,10 +105,13 @@ def test_lm_head_bit_identical_to_reference_kernel(reference_order, oracle, ref,
 
 @pytest.mark.parametrize("m", [32, 128, 2048])
 @pytest.mark.parametrize("k,n", QWEN_SHAPES)
-def test_prefill_gemm_bit_identical_to_reference_wmma(b200, oracle, ref, cuda, m, k, n):
+def test_prefill_gemm_bit_identical_to_reference_wmma(reference_order, oracle, ref, cuda, m,
+                                                       k, n):
     """The tcgen05 GEMMs (both precisions; W8A16 one-pass and dequantise-once
-    routes) against the reference WMMA kernels on the same buffers."""
+    routes) against the reference WMMA kernels on the same buffers (in the
+    reference order: the fast order splits K for short prompts)."""
     import torch
+    b200 = reference_order
     if n == 151936 and m > 128:
         pytest.skip("reference WMMA kernel at this size takes long; covered at M<=128")
     w, bb, _ = _case(oracle, n, k, seed=7 * n + k)
