@@ -218,9 +218,11 @@ def gemm_sweep(b200, device, reps=10):
     time per call, `reps` calls replayed from a CUDA graph (CUDA events).
     `weights`: "w8a16" = the default W8A16 path (one pass: no call
     allocates; M >= 1024 keeps the dequantised weights in tensor memory),
-    "bf16", and "w8a16_reserved" = W8A16 after b200_gemm_reserve_scratch
+    "bf16", and "w8a16_reserved" / "bf16_reserved" = after b200_gemm_reserve_scratch
     (dequantise once into the reserved buffer + BF16 GEMM) for the shapes
-    that route takes (M >= 1024 and M x N >= 2^25 outputs)."""
+    that route takes (M >= 1024 and M x N >= 2^25 outputs: dequantise once;
+    M <= 128 in the fast order: K split across the grid, partials in the
+    reserved buffer)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(99)
     mats = []
@@ -238,7 +240,7 @@ def gemm_sweep(b200, device, reps=10):
         y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
 
         def run():
-            if label == "bf16":
+            if label.startswith("bf16"):
                 b200.gemm_bf16(wb, bias, x, y, m, n, k)
             else:
                 b200.gemm_w8a16(q, s, 64, bias, x, y, m, n, k)
@@ -259,8 +261,10 @@ def gemm_sweep(b200, device, reps=10):
     if b200.ABI.b200_gemm_reserve_scratch(0) == 0:
         for (k, n, q, s, wb, bias) in mats:
             for m in PREFILL_M:
-                if m >= 1024 and m * n >= 32 * 1024 * 1024:
+                if (m >= 1024 and m * n >= 32 * 1024 * 1024) or m <= 128:
                     res.append(time_one("w8a16_reserved", k, n, q, s, wb, bias, m))
+                if m <= 128:
+                    res.append(time_one("bf16_reserved", k, n, q, s, wb, bias, m))
     del mats
     torch.cuda.empty_cache()
     return res
