@@ -29,6 +29,7 @@
 #include <cfloat>
 #include <climits>
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 
 #include "b200_linear.h"
@@ -855,7 +856,13 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   struct Cand { int lpr, r, wpr; };
   const Cand cands[] = {{8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1}, {32, 4, 1},
                         {32, 2, 1}, {32, 1, 1}, {32, 1, 2}, {32, 1, 4}};
+  // B200_GEMV_PLAN=lpr,r,wpr restricts the choice to that geometry (tuning).
+  int force_lpr = 0, force_r = 0, force_wpr = 0;
+  if (const char* e = getenv("B200_GEMV_PLAN")) {
+    sscanf(e, "%d,%d,%d", &force_lpr, &force_r, &force_wpr);
+  }
   for (const Cand& c : cands) {
+    if (force_lpr > 0 && (c.lpr != force_lpr || c.r != force_r || c.wpr != force_wpr)) continue;
     const int rows = c.wpr > 1 ? kConsumerWarps / c.wpr
                                : kConsumerWarps * (32 / c.lpr) * c.r;
     if (rows < min_rows) continue;
