@@ -117,6 +117,19 @@ int b200_engine_tokens(b200_engine_t engine, int* out, int count);
 /* Copies the BF16 logits of the last step to host memory (synchronises). */
 int b200_engine_logits(b200_engine_t engine, uint16_t* out);
 
+/* Causal GQA prefill attention of the engine on the tensor cores (head_dim
+ * 64): q rows [tokens][q_stride] BF16 with head h at column h*64 (RoPE
+ * applied), K / V caches [kv_heads][max_seq][64] BF16 holding positions
+ * [0, pos0 + tokens), out rows [tokens][out_stride] (head h at h*64); query
+ * t at position pos0 + t attends positions [0, pos0 + t].  FP32 scores and
+ * softmax, P rounded to BF16 for P.V, output BF16.  The reference computes
+ * the same attention with one CUDA-core block per (head, token)
+ * (src/cuda/kernels.cu:221-283, attention_prefill_bf16_kernel). */
+int b200_attention_prefill_bf16(const uint16_t* q, int q_stride, const uint16_t* kcache,
+                                const uint16_t* vcache, uint16_t* out, int out_stride,
+                                int tokens, int pos0, int heads, int kv_heads, int max_seq,
+                                b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,7 +21,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libb200linear.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["gemv.cu", "gemv_i8tc.cu", "gemm_simt.cu", "gemm_sm100.cu", "gemm_w8t.cu", "capi.cu", "noalloc.cu", "engine.cu",
+SOURCES = ["gemv.cu", "gemv_i8tc.cu", "gemm_simt.cu", "gemm_sm100.cu", "gemm_w8t.cu", "capi.cu", "noalloc.cu", "attention_tc.cu", "engine.cu",
            "decode_persistent.cu",
            "sharded.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

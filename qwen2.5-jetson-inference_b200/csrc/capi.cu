@@ -12,6 +12,7 @@ cudaError_t read_gemv_status(int* value, bool clear);    // gemv.cu
 cudaError_t read_comm_status(int* value, bool clear);    // sharded.cu
 cudaError_t read_w8t_status(int* value, bool clear);     // gemm_w8t.cu
 cudaError_t read_i8tc_status(int* value, bool clear);    // gemv_i8tc.cu
+cudaError_t read_att_status(int* value, bool clear);     // attention_tc.cu
 }
 
 using b200::bf16;
@@ -140,8 +141,11 @@ int b200_device_status(int clear) {
   int i8 = 0;
   if (e == cudaSuccess) e = b200::read_w8t_status(&w8t, clear != 0);
   if (e == cudaSuccess) e = b200::read_i8tc_status(&i8, clear != 0);
+  int att = 0;
+  if (e == cudaSuccess) e = b200::read_att_status(&att, clear != 0);
   if (e != cudaSuccess) return -int(e);
-  return gemm != 0 ? gemm : gemv != 0 ? gemv : comm != 0 ? comm : w8t != 0 ? w8t : i8;
+  return gemm != 0 ? gemm : gemv != 0 ? gemv : comm != 0 ? comm : w8t != 0 ? w8t : i8 != 0 ? i8
+                                                                                         : att;
 }
 
 int b200_gemv_bf16(const uint16_t* weight, const uint16_t* bias,

@@ -27,6 +27,8 @@
 #include <cfloat>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 #include <new>
 #include <vector>
 
@@ -260,6 +262,15 @@ int grid_for(size_t n) {
 using b200::bf16;
 
 namespace {
+// Prefill attention on the tensor cores from this many prompt tokens
+// (B200_ATTN_TC=1 / 0 forces it on / off).
+constexpr int kAttentionTcMinTokens = 64;
+bool use_attention_tc(int tokens) {
+  const char* e = getenv("B200_ATTN_TC");
+  if (e != nullptr) return strcmp(e, "1") == 0;
+  return tokens >= kAttentionTcMinTokens;
+}
+
 
 int check(cudaError_t e) { return e == cudaSuccess ? B200_OK : int(e); }
 
@@ -309,11 +320,17 @@ int layer_forward(b200_engine* e, int l, int t_rows, bool decode) {
   }
   ENGINE_TRY(launch(b200::rope_store_kernel, dim3(t_rows), dim3(256), 0, s, e->qkv, e->qkv_dim,
                     c.heads, c.kv_heads, hd, c.theta, 0, dpos, kc, vc, c.max_seq));
-  ENGINE_TRY(launch(b200::attention_kernel, dim3(c.heads, t_rows), dim3(128),
-                    b200::attend_smem_floats<128>(c.max_seq) * sizeof(float), s,
-                    (const bf16*)e->qkv, e->qkv_dim,
-                    (const bf16*)kc, (const bf16*)vc, e->att, c.heads, c.kv_heads, hd,
-                    c.max_seq, 0, dpos));
+  if (!decode && use_attention_tc(t_rows)) {
+    ENGINE_TRY(check(b200::launch_attention_prefill_tc(
+        (const bf16*)e->qkv, e->qkv_dim, (const bf16*)kc, (const bf16*)vc, e->att,
+        c.heads * hd, t_rows, 0, c.heads, c.kv_heads, c.max_seq, s)));
+  } else {
+    ENGINE_TRY(launch(b200::attention_kernel, dim3(c.heads, t_rows), dim3(128),
+                      b200::attend_smem_floats<128>(c.max_seq) * sizeof(float), s,
+                      (const bf16*)e->qkv, e->qkv_dim,
+                      (const bf16*)kc, (const bf16*)vc, e->att, c.heads, c.kv_heads, hd,
+                      c.max_seq, 0, dpos));
+  }
   if (decode) {
     b200::GemvFusion f;
     f.residual = e->x;
@@ -645,6 +662,23 @@ int b200_engine_decode(b200_engine_t e, int steps) {
     e->h_pos += 1;
   }
   return B200_OK;
+}
+
+int b200_attention_prefill_bf16(const uint16_t* q, int q_stride, const uint16_t* kcache,
+                                const uint16_t* vcache, uint16_t* out, int out_stride,
+                                int tokens, int pos0, int heads, int kv_heads, int max_seq,
+                                b200_stream_t stream) {
+  if (q == nullptr || kcache == nullptr || vcache == nullptr || out == nullptr || tokens < 0 ||
+      pos0 < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 ||
+      q_stride < heads * 64 || out_stride < heads * 64 || q_stride % 8 != 0 ||
+      out_stride % 8 != 0 || pos0 + tokens > max_seq) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  if (tokens == 0) return B200_OK;
+  return check(b200::launch_attention_prefill_tc(
+      reinterpret_cast<const bf16*>(q), q_stride, reinterpret_cast<const bf16*>(kcache),
+      reinterpret_cast<const bf16*>(vcache), reinterpret_cast<bf16*>(out), out_stride, tokens,
+      pos0, heads, kv_heads, max_seq, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int b200_engine_force_token(b200_engine_t e, int token) {

@@ -57,6 +57,14 @@ cudaError_t launch_gemv_i8tc(const void* weight, const bf16* scales, const bf16*
                              const bf16* input, bf16* output, int n, int k, float* block_value,
                              int* block_index, cudaStream_t stream, int* grid_out);
 
+// attention_tc.cu: causal GQA prefill attention on the tensor cores
+// (head_dim 64): q rows [tokens][q_stride] (head h at column h*64), caches
+// [kv_heads][max_seq][64], query t at position pos0 + t attends [0, pos0+t].
+cudaError_t launch_attention_prefill_tc(const bf16* q, int q_stride, const bf16* kcache,
+                                        const bf16* vcache, bf16* out, int out_stride, int tokens,
+                                        int pos0, int heads, int kv_heads, int max_seq,
+                                        cudaStream_t stream);
+
 // gemm_simt.cu: any shape / alignment, CUDA cores.
 cudaError_t launch_gemm_simt(bool w8, const void* weight, const bf16* scales,
                              const bf16* bias, const bf16* input, bf16* output,

@@ -144,3 +144,28 @@ def test_persistent_wait_timeout_is_reported_and_recoverable(mods):
     assert got == want
     assert e.device_status() == 0
     e.close()
+
+
+@pytest.mark.parametrize("tokens", [200, 250])
+def test_long_prompt_prefill_with_tensor_core_attention(mods, oracle, tokens, tmp_path):
+    """Prompts of >= 64 tokens take the tensor-core prefill attention
+    (csrc/attention_tc.cu): prefill logits against the reference engine with
+    its own kernels, cosine >= 0.9999, and the first token equal unless the
+    reference's top two logits are within two BF16 ulps."""
+    e2e, eng = mods
+    prompt = e2e.prompt_ids(tokens, seed=9)
+    try:
+        ref = e2e.run("reference", MODEL_DIR, prompt, precision="w16a16", new_tokens=1,
+                      warmup=0, repeat=1, logits_out=str(tmp_path / "r.bin"))
+    except FileNotFoundError as err:
+        pytest.skip(str(err))
+    e = eng.Engine(MODEL_DIR, "w16a16", max_seq=256, mode="graph")
+    toks, _, _ = e.generate(prompt, 1)
+    lg = oracle.bf16_to_f32(e.logits())
+    lr = np.fromfile(tmp_path / "r.bin", np.float32)
+    cos = float(lg @ lr / np.linalg.norm(lg) / np.linalg.norm(lr))
+    assert cos >= 0.9999, cos
+    top = np.sort(lr)[-2:]
+    assert toks[0] == ref["tokens"][0] or top[1] - top[0] <= 2 * 2.0 ** -7 * abs(top[1])
+    assert e.device_status() == 0
+    e.close()
