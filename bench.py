@@ -217,12 +217,12 @@ def gemm_sweep(b200, device, reps=10):
     """M x five shapes x {W8A16, BF16}.  `us` / TFLOP/s: device
     time per call, `reps` calls replayed from a CUDA graph (CUDA events).
     `weights`: "w8a16" = the default W8A16 path (one pass: no call
-    allocates; M >= 1024 keeps the dequantised weights in tensor memory),
+    allocates; the dequantised weights are kept in tensor memory),
     "bf16", and "w8a16_reserved" / "bf16_reserved" = after b200_gemm_reserve_scratch
     (dequantise once into the reserved buffer + BF16 GEMM) for the shapes
     that route takes (M >= 1024 and M x N >= 2^25 outputs: dequantise once;
-    M <= 128 in the fast order: K split across the grid, partials in the
-    reserved buffer)."""
+    M <= 128 and K >= 2048 in the fast order: K split across the grid,
+    partials in the reserved buffer)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(99)
     mats = []
@@ -253,18 +253,31 @@ def gemm_sweep(b200, device, reps=10):
         return {"weights": label, "m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
                 "tflops": round(2.0 * m * n * k / t / 1e12, 1)}
 
+    # The reservation is made first and the unreserved routes are selected
+    # per call (B200_GEMM_ONE_PASS / B200_GEMM_NO_SPLITK, read at every
+    # call), so each shape's rows are timed back to back under the same
+    # clocks instead of the reserved rows coming last, after the power-heavy
+    # long prompts.
+    reserved = b200.ABI.b200_gemm_reserve_scratch(0) == 0
+
+    def unreserved(fn):
+        os.environ["B200_GEMM_ONE_PASS"] = "1"
+        os.environ["B200_GEMM_NO_SPLITK"] = "1"
+        try:
+            return fn()
+        finally:
+            del os.environ["B200_GEMM_ONE_PASS"]
+            del os.environ["B200_GEMM_NO_SPLITK"]
+
     res = []
     for (k, n, q, s, wb, bias) in mats:
         for m in PREFILL_M:
-            res.append(time_one("w8a16", k, n, q, s, wb, bias, m))
-            res.append(time_one("bf16", k, n, q, s, wb, bias, m))
-    if b200.ABI.b200_gemm_reserve_scratch(0) == 0:
-        for (k, n, q, s, wb, bias) in mats:
-            for m in PREFILL_M:
-                if (m >= 1024 and m * n >= 32 * 1024 * 1024) or m <= 128:
-                    res.append(time_one("w8a16_reserved", k, n, q, s, wb, bias, m))
-                if m <= 128:
-                    res.append(time_one("bf16_reserved", k, n, q, s, wb, bias, m))
+            res.append(unreserved(lambda: time_one("w8a16", k, n, q, s, wb, bias, m)))
+            res.append(unreserved(lambda: time_one("bf16", k, n, q, s, wb, bias, m)))
+            if reserved and ((m >= 1024 and m * n >= 32 * 1024 * 1024) or m <= 128):
+                res.append(time_one("w8a16_reserved", k, n, q, s, wb, bias, m))
+            if reserved and m <= 128:
+                res.append(time_one("bf16_reserved", k, n, q, s, wb, bias, m))
     del mats
     torch.cuda.empty_cache()
     return res

@@ -1371,11 +1371,16 @@ splitk_reduce_kernel(const float* __restrict__ partial, int splits, const bf16* 
 // Short prompts in the fast summation order: the few output tiles each walk
 // K split over grid z (FP32 partials into the reserved buffer, reduced in a
 // fixed order).  Returns cudaErrorNotSupported when it does not apply.
+// Measured on B200: with K = 4864 the split halves a 32-token GEMM (32 ->
+// 16 us); with K = 896 the partial traffic and the extra launch cost more
+// than the split gains (e.g. 128 x 896 -> 896: 10.5 -> 22.9 us), so only
+// long K splits.
 constexpr int kSplitMaxTokens = 128;
+constexpr int kSplitMinK = 2048;
 cudaError_t gemm_split_k(bool w8, const void* weight, const bf16* scales, const bf16* bias,
                          const bf16* input, bf16* output, int m, int n, int k, int ldc,
                          cudaStream_t stream) {
-  if (m > kSplitMaxTokens || summation_order() != B200_ORDER_FAST ||
+  if (m > kSplitMaxTokens || k < kSplitMinK || summation_order() != B200_ORDER_FAST ||
       getenv("B200_GEMM_NO_SPLITK") != nullptr) {
     return cudaErrorNotSupported;
   }
@@ -1432,6 +1437,13 @@ cudaError_t reserve_gemm_scratch(size_t bytes) {
   return scratch_get(bytes == 0 ? kScratchCap : bytes, true, &sc);
 }
 
+// Prompts of < 1024 tokens on the TMEM-weight kernel unless
+// B200_GEMM_W8T_SHORT=0 (read at every call, for measurement).
+static bool use_w8t_short() {
+  const char* e = getenv("B200_GEMM_W8T_SHORT");
+  return e == nullptr || strcmp(e, "0") != 0;
+}
+
 cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales,
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
@@ -1452,10 +1464,13 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                               stream);
     }
   }
-  // One pass with the dequantised weights in TMEM for long prompts
-  // (gemm_w8t.cu); its epilogue has no peer stores, so the sharded form keeps
-  // the shared-memory dequant kernels.
-  if (w8 && peers.n == 0 && (m >= kTwoPassMinTokens || use_w8t()) &&
+  // One pass with the dequantised weights in TMEM (gemm_w8t.cu) at every
+  // prompt length (short prompts get a token tile fitted to them: the
+  // weights stay the MMA's M side, no token padding to 128; measured faster
+  // than the shared-memory dequant kernel at 32, 128 and 512 tokens, 2x on
+  // 896 -> 151936); its epilogue has no peer stores, so the sharded form
+  // keeps the shared-memory dequant kernels.
+  if (w8 && peers.n == 0 && (m >= kTwoPassMinTokens || use_w8t_short() || use_w8t()) &&
       gemm_w8t_supported(weight, input, output, m, n, k)) {
     return launch_gemm_w8t(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }

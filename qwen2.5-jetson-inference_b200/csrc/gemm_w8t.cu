@@ -450,13 +450,24 @@ cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* 
                             const bf16* input, bf16* output, int m, int n, int k, int ldc,
                             cudaStream_t stream) {
   // Tile shape: tokens per tile x quantisation groups per stage
-  // (B200_W8T_CFG=192x2 | 192x1 | 128x2 | 128x1 overrides, for tuning).
+  // (B200_W8T_CFG=192x2 | 192x1 | 160x2 | 128x2 | 128x1 | 96x2 | 64x2 | 32x2 overrides, for
+  // tuning; 160x2 leaves TMEM room for three A slots, 96x2 for five; 64x2 and
+  // 32x2 for short prompts).
   const char* cfg = getenv("B200_W8T_CFG");
   if (cfg != nullptr) {
     if (!strcmp(cfg, "192x1")) return launch_bt<192, 1>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     if (!strcmp(cfg, "128x1")) return launch_bt<128, 1>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     if (!strcmp(cfg, "128x2")) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "160x2")) return launch_bt<160, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "96x2")) return launch_bt<96, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "64x2")) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "32x2")) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }
+  // Short prompts: the smallest token tile that covers them (no padding of
+  // the MMA's N to 192).
+  if (m <= 32) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  if (m <= 64) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  if (m <= 128) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   return launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
 }
 

@@ -875,7 +875,13 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
     const double eff = double(chunks) / double(iters * span);
     const int tiles = (n + rows - 1) / rows;
     const int waves = (tiles + sms - 1) / sms;
-    const double cost = double(waves) * rows * row_bytes / eff +
+    // Large W8 matrices at in_features 896: two rows per lane (16 lanes a
+    // row) measured 2.7% faster than one (27.6 vs 28.4 us on 896 -> 151936)
+    // although a lane's 3.5 chunks leave lanes idle; 32 lanes with x in
+    // registers, or 4 rows a lane, measured slower (32-40 us).
+    const double shape_factor =
+        (w8 && k == 896 && n >= 16384 && !(c.lpr == 16 && c.r == 2)) ? 1.2 : 1.0;
+    const double cost = double(waves) * rows * row_bytes / eff * shape_factor +
                         (c.wpr > 1 ? waves * 2048.0 : 0.0);
     if (cost < best_cost * 0.999) {
       best_cost = cost;

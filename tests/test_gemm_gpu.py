@@ -188,3 +188,51 @@ def test_w8a16_one_pass_and_two_pass_agree(b200, oracle, cuda, m, k, n):
     exp = oracle.bf16_to_f32(oracle.linear_w8a16(qn, sn, bb, xb, gemm=True))
     got = a[rows].cpu().numpy()
     assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
+
+
+@pytest.mark.parametrize("m,k,n", [(32, 4864, 896), (128, 4864, 896), (7, 2112, 264),
+                                   (96, 8192, 128)])
+@pytest.mark.parametrize("w8", [True, False], ids=["w8a16", "bf16"])
+def test_short_prompt_split_k(b200, oracle, cuda, m, k, n, w8):
+    """Fast order, <= 128 tokens, K >= 2048, with a reservation: K splits
+    across grid z with FP32 partials and a fixed-order reduce.  Every row
+    against the oracle; the unsplit kernel (B200_GEMM_NO_SPLITK) on the same
+    inputs within one BF16 ulp; two runs bit-identical."""
+    import os
+    import torch
+    assert b200.ABI.b200_gemm_reserve_scratch(0) == 0
+    rng = np.random.default_rng(m * 31 + k + n)
+    w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+    bb = oracle.f32_to_bf16(rng.normal(0, 0.02, n).astype(np.float32))
+    xb = oracle.f32_to_bf16(rng.standard_normal((m, k)).astype(np.float32))
+    dx, db = from_bits(xb, cuda), from_bits(bb, cuda)
+    if w8:
+        q, sb = oracle.quantize_groupwise(w)
+        dq, ds = torch.from_numpy(q).to(cuda), from_bits(sb, cuda)
+        exp = oracle.bf16_to_f32(oracle.linear_w8a16(q, sb, bb, xb, gemm=True))
+
+        def call(y):
+            b200.gemm_w8a16(dq, ds, 64, db, dx, y, m, n, k)
+    else:
+        wb = oracle.f32_to_bf16(w)
+        dw = from_bits(wb, cuda)
+        exp = oracle.bf16_to_f32(oracle.f32_to_bf16(oracle.linear_bf16(wb, bb, xb)))
+
+        def call(y):
+            b200.gemm_bf16(dw, db, dx, y, m, n, k)
+    ys = [torch.empty(m, n, dtype=torch.bfloat16, device=cuda) for _ in range(3)]
+    call(ys[0])
+    call(ys[1])
+    os.environ["B200_GEMM_NO_SPLITK"] = "1"
+    try:
+        call(ys[2])
+    finally:
+        del os.environ["B200_GEMM_NO_SPLITK"]
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[1])
+    got = oracle.bf16_to_f32(to_bits(ys[0]))
+    ulp = np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4
+    assert np.all(np.abs(got - exp) <= ulp)
+    unsplit = oracle.bf16_to_f32(to_bits(ys[2]))
+    assert np.all(np.abs(got - unsplit) <= np.abs(unsplit) * 2.0 ** -7 * 1.01 + 1e-4)
+    assert b200.device_status() == 0
