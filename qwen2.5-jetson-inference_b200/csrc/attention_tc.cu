@@ -79,7 +79,7 @@ attention_prefill_tc_kernel(const bf16* __restrict__ q, int q_stride, const bf16
   const int head = blockIdx.x;
   const int q0 = blockIdx.y * kQ;
   const int kvh = head / (heads / kv_heads);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const bf16* kb = kcache + size_t(kvh) * max_seq * kD;
   const bf16* vb = vcache + size_t(kvh) * max_seq * kD;
 

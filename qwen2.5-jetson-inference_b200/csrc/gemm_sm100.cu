@@ -1439,6 +1439,12 @@ cudaError_t reserve_gemm_scratch(size_t bytes) {
 
 // Prompts of < 1024 tokens on the TMEM-weight kernel unless
 // B200_GEMM_W8T_SHORT=0 (read at every call, for measurement).
+static bool use_w16t(int m, int n, int k) {
+  const char* e = getenv("B200_GEMM_W16T");
+  if (e != nullptr) return strcmp(e, "1") == 0;
+  return m <= 32 || n >= 16384 || k >= 2048;
+}
+
 static bool use_w8t_short() {
   const char* e = getenv("B200_GEMM_W8T_SHORT");
   return e == nullptr || strcmp(e, "0") != 0;
@@ -1473,6 +1479,16 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
   if (w8 && peers.n == 0 && (m >= kTwoPassMinTokens || use_w8t_short() || use_w8t()) &&
       gemm_w8t_supported(weight, input, output, m, n, k)) {
     return launch_gemm_w8t(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  }
+  // BF16, <= 128 tokens: the transposed form (weights the MMA's M side,
+  // token tile fitted to the prompt) where it measured faster: <= 32 tokens
+  // (e.g. 32 x 896 -> 151936: 60.7 -> 47.6 us), and up to 128 tokens for
+  // wide or long-K matrices (128 x 896 -> 4864 stays on the default kernel:
+  // 7.3 vs 8.6 us).  B200_GEMM_W16T=1 / 0 forces it on / off.
+  if (!w8 && peers.n == 0 && m <= 128 && use_w16t(m, n, k) &&
+      gemm_w8t_supported(weight, input, output, m, n, k)) {
+    return launch_gemm_w16t(static_cast<const bf16*>(weight), bias, input, output, m, n, k,
+                            ldc, stream);
   }
   const Tile t = choose_tile(w8, m, n);
   return w8 ? launch_tile<true>(t, weight, scales, bias, input, output, m, n, k, ldc, peers,

@@ -66,26 +66,30 @@ constexpr int kBK = 64;      // K per k-block = one quantisation group
 // kSub: quantisation groups (64 K values) per pipeline stage, 1 or 2.  The
 // MMA issuer pays a fixed ~300-500 cycles per barrier wait (measured), so a
 // stage must carry enough MMA work to keep the tensor pipe busy meanwhile.
-template <int kBT, int kSub>
+// kW16: BF16 weights, loaded by TMA as [128 x 64] 128-byte-swizzled
+// sub-tiles and read by the MMA from shared memory (no dequantiser warps,
+// no A slots in TMEM); the rest of the kernel is shared.
+template <int kBT, int kSub, bool kW16 = false>
 struct CfgT {
   static constexpr int kKS = kBK * kSub;                  // K per stage
-  static constexpr int kDqWarps = 8;                      // 2 per lane quarter
+  static constexpr int kDqWarps = kW16 ? 0 : 8;           // 2 per lane quarter
   static constexpr int kXSub = kBT * kBK * 2;             // one 64-wide X sub-tile
   static constexpr int kXBytes = kSub * kXSub;
-  static constexpr int kQBytes = kRows * kKS;             // 128 x kKS INT8
+  static constexpr int kWSub = kRows * kBK * 2;           // one BF16 W sub-tile
+  static constexpr int kQBytes = kW16 ? kSub * kWSub : kRows * kKS;  // W tile
   static constexpr int kStageBytes = kXBytes + kQBytes;
   static constexpr int kStages =
       (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
   static constexpr int kAccCols = kBT;
   static constexpr int kACols = kKS / 2;                  // BF16 pairs per slot
   static constexpr int kAStages =
-      (512 - 2 * kAccCols) / kACols > 8 ? 8 : (512 - 2 * kAccCols) / kACols;
+      kW16 ? 1 : ((512 - 2 * kAccCols) / kACols > 8 ? 8 : (512 - 2 * kAccCols) / kACols);
   static constexpr int kACol0 = 2 * kAccCols;
   static constexpr int kThreads = (8 + kDqWarps) * 32;
   static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
   static_assert(kSub == 1 || kSub == 2, "one or two groups per stage");
   static_assert(kBT % 16 == 0 && kBT >= 16 && kBT <= 256, "MMA N");
-  static_assert(kAStages >= 2 && kStages >= 2, "ring sizes");
+  static_assert((kW16 || kAStages >= 2) && kStages >= 2, "ring sizes");
   static_assert(kXSub % 1024 == 0, "128B-swizzle atoms");
 };
 
@@ -114,13 +118,13 @@ __device__ __forceinline__ void dq4(uint32_t word, bf162 s2, uint32_t* out) {
   out[1] = *reinterpret_cast<const uint32_t*>(&d23);
 }
 
-template <int kBT, int kSub>
-__global__ void __launch_bounds__(CfgT<kBT, kSub>::kThreads, 1)
+template <int kBT, int kSub, bool kW16>
+__global__ void __launch_bounds__(CfgT<kBT, kSub, kW16>::kThreads, 1)
 gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_q,
                 const uint16_t* __restrict__ scales, const bf16* __restrict__ bias,
                 bf16* __restrict__ out, int m, int n, int k, int ldc) {
-  using C = CfgT<kBT, kSub>;
+  using C = CfgT<kBT, kSub, kW16>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -150,7 +154,7 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
       mbar_init(bar_empty + 8 * s, 1 + C::kDqWarps);  // MMA commit + dequant warps
     }
     for (int a = 0; a < C::kAStages; ++a) {
-      mbar_init(bar_afull + 8 * a, C::kDqWarps);
+      mbar_init(bar_afull + 8 * a, C::kDqWarps > 0 ? C::kDqWarps : 1);  // unused: kW16
       mbar_init(bar_aempty + 8 * a, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -196,7 +200,15 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
             tma_load_2d(smem_u32(st + sub * C::kXSub), &tmap_x, kb * C::kKS + sub * kBK,
                         mb * kBT, fb);
           }
-          tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS, nb * kRows, fb);
+          if constexpr (kW16) {
+#pragma unroll
+            for (int sub = 0; sub < kSub; ++sub) {
+              tma_load_2d(smem_u32(st + C::kXBytes + sub * C::kWSub), &tmap_q,
+                          kb * C::kKS + sub * kBK, nb * kRows, fb);
+            }
+          } else {
+            tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS, nb * kRows, fb);
+          }
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -224,22 +236,34 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
           // The dequant warps arrive on a_full only after they waited for
           // this step's stage (X and INT8 land on the same barrier), so a_full
           // also orders the X tile: one wait per k-block.
-          if (!wait_t(bar_afull + 8 * aslot, aphase, abort_flag,
-                      B200_DEVICE_TIMEOUT_PIPELINE)) {
+          // kW16: the stage's own full barrier (X and W land on it).
+          if (!wait_t(kW16 ? bar_full + 8 * stage : bar_afull + 8 * aslot,
+                      kW16 ? phase : aphase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t x_addr = smem_u32(smem + stage * C::kStageBytes);
-          const uint32_t a_addr = tmem_base + uint32_t(C::kACol0 + aslot * C::kACols);
+          if constexpr (kW16) {
+            const uint32_t w_addr = x_addr + C::kXBytes;
 #pragma unroll
-          for (int kk = 0; kk < C::kKS / 16; ++kk) {
-            mma_bf16_ta(d_addr, a_addr + uint32_t(kk * 8),
-                        desc_sw128(x_addr + (kk >> 2) * C::kXSub + (kk & 3) * 32), idesc,
-                        (kb > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < C::kKS / 16; ++kk) {
+              mma_bf16(d_addr, desc_sw128(w_addr + (kk >> 2) * C::kWSub + (kk & 3) * 32),
+                       desc_sw128(x_addr + (kk >> 2) * C::kXSub + (kk & 3) * 32), idesc,
+                       (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(bar_empty + 8 * stage);
+          } else {
+            const uint32_t a_addr = tmem_base + uint32_t(C::kACol0 + aslot * C::kACols);
+#pragma unroll
+            for (int kk = 0; kk < C::kKS / 16; ++kk) {
+              mma_bf16_ta(d_addr, a_addr + uint32_t(kk * 8),
+                          desc_sw128(x_addr + (kk >> 2) * C::kXSub + (kk & 3) * 32), idesc,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(bar_empty + 8 * stage);
+            mma_commit(bar_aempty + 8 * aslot);
           }
-          mma_commit(bar_empty + 8 * stage);
-          mma_commit(bar_aempty + 8 * aslot);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -306,7 +330,7 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
       tc_fence_before();
       mbar_arrive(bar_acc_empty + 8 * buf);
     }
-  } else if (warp >= 8) {
+  } else if (!kW16 && warp >= 8) {
     // ---------------------------------------------------------- dequantiser
     // Warps w and w+4 cover TMEM lane quarter w % 4 and split each stage's K
     // range in two parts (part p: kKS/2 values = one group when kSub == 2).
@@ -395,16 +419,20 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
-template <int kBT, int kSub>
+template <int kBT, int kSub, bool kW16 = false>
 cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
                       const bf16* input, bf16* output, int m, int n, int k, int ldc,
                       cudaStream_t stream) {
-  using C = CfgT<kBT, kSub>;
+  using C = CfgT<kBT, kSub, kW16>;
   CUtensorMap tx, tq;
   if (!encode_tmap_2d(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, kBT,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, C::kKS, kRows,
-                      kSub == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)) {
+      !(kW16 ? encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK,
+                              kRows, CU_TENSOR_MAP_SWIZZLE_128B)
+             : encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, C::kKS,
+                              kRows,
+                              kSub == 1 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                        : CU_TENSOR_MAP_SWIZZLE_128B))) {
     return cudaErrorInvalidValue;
   }
   static std::atomic<unsigned long long> attr_done{0};
@@ -413,7 +441,7 @@ cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
   const unsigned long long bit = (dev >= 0 && dev < 64) ? 1ull << dev : 0ull;
   if (bit == 0 || (attr_done.load(std::memory_order_acquire) & bit) == 0) {
     const cudaError_t e = cudaFuncSetAttribute(
-        gemm_w8t_kernel<kBT, kSub>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        gemm_w8t_kernel<kBT, kSub, kW16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
         C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_release);
@@ -432,7 +460,7 @@ cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_w8t_kernel<kBT, kSub>, tx, tq,
+  return cudaLaunchKernelEx(&cfg, gemm_w8t_kernel<kBT, kSub, kW16>, tx, tq,
                             reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k,
                             ldc);
 }
@@ -469,6 +497,17 @@ cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* 
   if (m <= 64) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   if (m <= 128) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   return launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+}
+
+// BF16 weights in the same transposed form (weights the MMA's M side from
+// shared memory, tokens its N side): for prompts of <= 128 tokens, whose
+// token tile is then 32 / 64 / 128 instead of padding to 128 tokens x a
+// narrow weight tile.
+cudaError_t launch_gemm_w16t(const bf16* weight, const bf16* bias, const bf16* input,
+                             bf16* output, int m, int n, int k, int ldc, cudaStream_t stream) {
+  if (m <= 32) return launch_bt<32, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
+  if (m <= 64) return launch_bt<64, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
+  return launch_bt<128, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
 }
 
 }  // namespace b200

@@ -97,6 +97,10 @@ bool gemm_w8t_supported(const void* weight, const void* input, const void* outpu
 cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* bias,
                             const bf16* input, bf16* output, int m, int n, int k, int ldc,
                             cudaStream_t stream);
+// The same transposed form with BF16 weights read by the MMA from shared
+// memory (same support conditions), for prompts of <= 128 tokens.
+cudaError_t launch_gemm_w16t(const bf16* weight, const bf16* bias, const bf16* input,
+                             bf16* output, int m, int n, int k, int ldc, cudaStream_t stream);
 
 // Allocates (once per device) the BF16 weight buffer of the two-pass W8A16
 // prefill path; bytes == 0 means the default cap.

@@ -236,3 +236,37 @@ def test_short_prompt_split_k(b200, oracle, cuda, m, k, n, w8):
     unsplit = oracle.bf16_to_f32(to_bits(ys[2]))
     assert np.all(np.abs(got - unsplit) <= np.abs(unsplit) * 2.0 ** -7 * 1.01 + 1e-4)
     assert b200.device_status() == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(32, 896, 151936), (128, 896, 4864), (7, 896, 896),
+                                   (64, 4864, 896), (100, 1088, 264)])
+def test_bf16_transposed_form_matches_default(b200, oracle, cuda, m, k, n):
+    """BF16 GEMM for <= 128 tokens in the transposed form (weights the MMA's
+    M side, B200_GEMM_W16T=1) against the CTA-tile kernel (=0) on the same inputs
+    (bit-identical: same products, same K order) and the oracle."""
+    import os
+    import torch
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m * 7 + n)
+    w = (torch.randn(n, k, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g, device=cuda).to(torch.bfloat16)
+    ref = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    got = torch.empty_like(ref)
+    try:
+        os.environ["B200_GEMM_W16T"] = "0"
+        b200.gemm_bf16(w, bias, x, ref, m, n, k)
+        os.environ["B200_GEMM_W16T"] = "1"
+        b200.gemm_bf16(w, bias, x, got, m, n, k)
+    finally:
+        del os.environ["B200_GEMM_W16T"]
+    torch.cuda.synchronize()
+    assert b200.device_status() == 0
+    assert torch.equal(got, ref), float((got.float() - ref.float()).abs().max())
+    rows = [0, m // 2, m - 1]
+    wb = w.view(torch.int16).cpu().numpy().view(np.uint16)
+    xb = x[rows].view(torch.int16).cpu().numpy().view(np.uint16)
+    bb = bias.view(torch.int16).cpu().numpy().view(np.uint16)
+    exp = oracle.bf16_to_f32(oracle.f32_to_bf16(oracle.linear_bf16(wb, bb, xb)))
+    g32 = got[rows].float().cpu().numpy()
+    assert np.all(np.abs(g32 - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
