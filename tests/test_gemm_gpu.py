@@ -270,3 +270,39 @@ def test_bf16_transposed_form_matches_default(b200, oracle, cuda, m, k, n):
     exp = oracle.bf16_to_f32(oracle.f32_to_bf16(oracle.linear_bf16(wb, bb, xb)))
     g32 = got[rows].float().cpu().numpy()
     assert np.all(np.abs(g32 - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
+
+
+@pytest.mark.parametrize("m,k,n", [(2048, 896, 4864), (1000, 1088, 1000), (200, 896, 300),
+                                   (1200, 4864, 896)])
+def test_w8a16_cta_pair_form_matches_one_sm_form(b200, oracle, cuda, m, k, n):
+    """The CTA-pair W8A16 kernel (cta_group::2: A from each SM's TMEM, X split
+    between the pair; B200_W8T_CFG=p192) gives the same bits as the one-SM
+    kernel (192x2) on the same inputs, ragged sizes included, and matches the
+    oracle on sampled rows."""
+    import os
+    import torch
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m + 3 * n)
+    w = torch.randn(n, k, generator=g, device=cuda) * 0.02
+    q, s = b200.quantize_groupwise(w)
+    bias = (torch.randn(n, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g, device=cuda).to(torch.bfloat16)
+    ys = []
+    try:
+        for cfg in ("192x2", "p192", "p192"):
+            os.environ["B200_W8T_CFG"] = cfg
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+            b200.gemm_w8a16(q, s, 64, bias, x, y, m, n, k)
+            ys.append(y)
+    finally:
+        del os.environ["B200_W8T_CFG"]
+    torch.cuda.synchronize()
+    assert b200.device_status() == 0
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+    rows = [0, m // 2, m - 1]
+    qn, sn = q.cpu().numpy(), s.view(torch.int16).cpu().numpy().view(np.uint16)
+    xb = x[rows].view(torch.int16).cpu().numpy().view(np.uint16)
+    bb = bias.view(torch.int16).cpu().numpy().view(np.uint16)
+    exp = oracle.bf16_to_f32(oracle.linear_w8a16(qn, sn, bb, xb, gemm=True))
+    got = ys[1][rows].float().cpu().numpy()
+    assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
