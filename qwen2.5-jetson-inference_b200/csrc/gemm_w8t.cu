@@ -899,6 +899,11 @@ cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* 
   // the MMA's N to 192).
   if (m <= 32) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   if (m <= 64) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  // 65..128 tokens: two 64-token tiles when the weight tiles alone leave
+  // most SMs idle (128 x 896 -> 4864: 10.25 -> 8.62 us).
+  if (m <= 128 && (n + kRows - 1) / kRows < 74) {
+    return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  }
   if (m <= 128) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
   // Long prompts up to 2^29 outputs: the CTA-pair form, measured 2-6% faster
   // (e.g. 8192 x 4864 -> 896: 92.4 -> 87.3 us); 10% slower at 8192 x 896 ->
