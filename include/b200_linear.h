@@ -141,6 +141,27 @@ int b200_gemm_w8a16(const int8_t* weight, const uint16_t* scales,
  * src/qwen2.cpp:80-200). */
 int b200_gemm_reserve_scratch(size_t bytes);
 
+/* Weight pre-packing at upload (W8A16).  The reference uploads the INT8
+ * weights as they are, row-major [N, K] (src/qwen2.cpp:56-78), and its notes
+ * name packing at upload as the place for kernel-specific layouts
+ * (docs/architecture.md:36).  b200_pack_w8a16 re-tiles them once into
+ * [2 ceil(N/256)][ceil(K/128)] blocks of 16 KB.  Each block is 128 rows x
+ * 128 K values in the 128-byte-swizzled layout the prefill kernels hold in
+ * shared memory.  Blocks are zero-filled outside the matrix.
+ * b200_gemm_w8a16_packed then fetches each block with one contiguous bulk
+ * copy instead of a box of rows strided by K.  Scales stay in the reference
+ * layout.  Results are bit-identical to b200_gemm_w8a16.
+ * Requirements: in_features % 16 == 0; weight, packed and input 16-byte
+ * aligned.  The packed buffer (b200_w8a16_packed_bytes) is the caller's;
+ * packing runs asynchronously on `stream`. */
+size_t b200_w8a16_packed_bytes(int out_features, int in_features);
+int b200_pack_w8a16(const int8_t* weight, int out_features, int in_features, void* packed,
+                    b200_stream_t stream);
+int b200_gemm_w8a16_packed(const void* packed, const uint16_t* scales, int group_size,
+                           const uint16_t* bias, const uint16_t* input, uint16_t* output,
+                           int tokens, int out_features, int in_features,
+                           b200_stream_t stream);
+
 /* Bytes of workspace b200_lm_head_* need, split as the reference splits it:
  * ceil(vocab/8) floats followed by ceil(vocab/8) ints
  * (reference src/qwen2.cpp:193-198).  The kernels use at most that much. */

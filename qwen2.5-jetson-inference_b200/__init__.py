@@ -43,6 +43,9 @@ _SIGNATURES = {
     "b200_lm_head_w8a16": ([_p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p], _i),
     "b200_argmax_bf16": ([_p, _i, _p, _p], _i),
     "b200_gemm_reserve_scratch": ([ctypes.c_size_t], _i),
+    "b200_w8a16_packed_bytes": ([_i, _i], ctypes.c_size_t),
+    "b200_pack_w8a16": ([_p, _i, _i, _p, _p], _i),
+    "b200_gemm_w8a16_packed": ([_p, _p, _i, _p, _p, _p, _i, _i, _i, _p], _i),
     "b200_lm_head_noalloc_max_vocab": ([], ctypes.c_size_t),
     "b200_lm_head_bf16_noalloc": ([_p, _p, _p, _p, _p, _i, _i, _p], _i),
     "b200_set_summation_order": ([_i], _i),
@@ -152,6 +155,25 @@ def gemm_w8a16(weight, scales, group_size, bias, input, output, tokens,
                                 _ptr(input), _ptr(output), tokens, out_features,
                                 in_features, _stream(stream)),
            "gemm_w8a16")
+
+
+def pack_w8a16(weight, out_features, in_features, stream=None):
+    """Pre-packs INT8 weights [N, K] once at upload into the prefill
+    kernels' tile layout (b200_pack_w8a16); returns the packed uint8 tensor."""
+    nbytes = int(_lib.b200_w8a16_packed_bytes(out_features, in_features))
+    packed = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=weight.device)
+    _check(_lib.b200_pack_w8a16(_ptr(weight), out_features, in_features, _ptr(packed),
+                                _stream(stream)), "pack_w8a16")
+    return packed
+
+
+def gemm_w8a16_packed(packed, scales, group_size, bias, input, output, tokens,
+                      out_features, in_features, stream=None):
+    """gemm_w8a16 on weights pre-packed by pack_w8a16 (bit-identical)."""
+    _check(_lib.b200_gemm_w8a16_packed(_ptr(packed), _ptr(scales), group_size, _ptr(bias),
+                                       _ptr(input), _ptr(output), tokens, out_features,
+                                       in_features, _stream(stream)),
+           "gemm_w8a16_packed")
 
 
 def lm_head_workspace_bytes(vocab: int, in_features: int) -> int:

@@ -234,3 +234,43 @@ int b200_argmax_bf16(const uint16_t* values, int n, int* output,
 }
 
 }  // extern "C"
+
+extern "C" {
+
+size_t b200_w8a16_packed_bytes(int out_features, int in_features) {
+  return b200::w8a16_packed_bytes(out_features, in_features);
+}
+
+int b200_pack_w8a16(const int8_t* weight, int out_features, int in_features, void* packed,
+                    b200_stream_t stream) {
+  if (out_features < 0 || in_features < 0) return B200_ERR_INVALID_ARGUMENT;
+  if (out_features == 0 || in_features == 0) return B200_OK;
+  if (weight == nullptr || packed == nullptr || in_features % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(weight) & 15u) != 0 ||
+      (reinterpret_cast<uintptr_t>(packed) & 15u) != 0) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  return status_of(b200::launch_pack_w8a16(weight, out_features, in_features, packed,
+                                           static_cast<cudaStream_t>(stream)));
+}
+
+int b200_gemm_w8a16_packed(const void* packed, const uint16_t* scales, int group_size,
+                           const uint16_t* bias, const uint16_t* input, uint16_t* output,
+                           int tokens, int out_features, int in_features,
+                           b200_stream_t stream) {
+  if (group_size != 64) return B200_ERR_GROUP_SIZE;
+  int rc = check_linear_args(packed, input, output, tokens, out_features, in_features);
+  if (rc != B200_OK) return rc;
+  if (tokens == 0 || out_features == 0) return B200_OK;
+  if (in_features == 0 || scales == nullptr || in_features % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(packed) & 15u) != 0 ||
+      (reinterpret_cast<uintptr_t>(input) & 15u) != 0) {
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  return status_of(b200::launch_gemm_w8t(packed, as_bf16(scales), as_bf16(bias),
+                                         as_bf16(input), as_bf16(output), tokens,
+                                         out_features, in_features, out_features,
+                                         static_cast<cudaStream_t>(stream), packed));
+}
+
+}  // extern "C"

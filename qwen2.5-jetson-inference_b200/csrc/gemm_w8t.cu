@@ -123,7 +123,8 @@ __global__ void __launch_bounds__(CfgT<kBT, kSub, kW16>::kThreads, 1)
 gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_q,
                 const uint16_t* __restrict__ scales, const bf16* __restrict__ bias,
-                bf16* __restrict__ out, int m, int n, int k, int ldc) {
+                bf16* __restrict__ out, int m, int n, int k, int ldc,
+                const unsigned char* __restrict__ packed) {
   using C = CfgT<kBT, kSub, kW16>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -206,6 +207,11 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
               tma_load_2d(smem_u32(st + C::kXBytes + sub * C::kWSub), &tmap_q,
                           kb * C::kKS + sub * kBK, nb * kRows, fb);
             }
+          } else if (kSub == 2 && packed != nullptr) {
+            // Pre-packed weights: the tile's shared-memory image is one
+            // contiguous 16 KB block (b200_pack_w8a16).
+            bulk_load(smem_u32(st + C::kXBytes),
+                      packed + (size_t(nb) * num_kb + kb) * C::kQBytes, C::kQBytes, fb);
           } else {
             tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS, nb * kRows, fb);
           }
@@ -422,7 +428,7 @@ gemm_w8t_kernel(const __grid_constant__ CUtensorMap tmap_x,
 template <int kBT, int kSub, bool kW16 = false>
 cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
                       const bf16* input, bf16* output, int m, int n, int k, int ldc,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const void* packed = nullptr) {
   using C = CfgT<kBT, kSub, kW16>;
   CUtensorMap tx, tq;
   if (!encode_tmap_2d(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, kBT,
@@ -462,7 +468,7 @@ cudaError_t launch_bt(const void* weight, const bf16* scales, const bf16* bias,
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, gemm_w8t_kernel<kBT, kSub, kW16>, tx, tq,
                             reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k,
-                            ldc);
+                            ldc, static_cast<const unsigned char*>(packed));
 }
 
 // ===================================================================
@@ -533,7 +539,8 @@ __global__ void __launch_bounds__(CfgP<kBT>::kThreads, 1)
 gemm_w8t2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_q,
                  const uint16_t* __restrict__ scales, const bf16* __restrict__ bias,
-                 bf16* __restrict__ out, int m, int n, int k, int ldc) {
+                 bf16* __restrict__ out, int m, int n, int k, int ldc,
+                 const unsigned char* __restrict__ packed) {
   using C = CfgP<kBT>;
   extern __shared__ __align__(1024) unsigned char smem_rawp[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -613,8 +620,14 @@ gemm_w8t2_kernel(const __grid_constant__ CUtensorMap tmap_x,
             tma_load_2d_pair(smem_u32(st + sub * C::kXSub), &tmap_x, kb * C::kKS + sub * kBK,
                              mb * kBT + int(rank) * C::kXHalf, fb);
           }
-          tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS,
-                      nb * 2 * kRows + int(rank) * kRows, fb);
+          if (packed != nullptr) {
+            bulk_load(smem_u32(st + C::kXBytes),
+                      packed + (size_t(nb * 2 + int(rank)) * num_kb + kb) * C::kQBytes,
+                      C::kQBytes, fb);
+          } else {
+            tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS,
+                        nb * 2 * kRows + int(rank) * kRows, fb);
+          }
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -823,7 +836,7 @@ gemm_w8t2_kernel(const __grid_constant__ CUtensorMap tmap_x,
 template <int kBT>
 cudaError_t launch_pair_bt(const void* weight, const bf16* scales, const bf16* bias,
                            const bf16* input, bf16* output, int m, int n, int k, int ldc,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, const void* packed = nullptr) {
   using C = CfgP<kBT>;
   CUtensorMap tx, tq;
   if (!encode_tmap_2d(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, C::kXHalf,
@@ -863,7 +876,7 @@ cudaError_t launch_pair_bt(const void* weight, const bf16* scales, const bf16* b
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, gemm_w8t2_kernel<kBT>, tx, tq,
                             reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k,
-                            ldc);
+                            ldc, static_cast<const unsigned char*>(packed));
 }
 
 }  // namespace
@@ -877,41 +890,41 @@ bool gemm_w8t_supported(const void* weight, const void* input, const void* outpu
 
 cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* bias,
                             const bf16* input, bf16* output, int m, int n, int k, int ldc,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, const void* packed) {
   // Tile shape: tokens per tile x quantisation groups per stage
   // (B200_W8T_CFG=192x2 | 192x1 | 160x2 | 128x2 | 128x1 | 96x2 | 64x2 | 32x2 | p192 | p128
   // overrides, for
   // tuning; 160x2 leaves TMEM room for three A slots, 96x2 for five; 64x2 and
   // 32x2 for short prompts).
   const char* cfg = getenv("B200_W8T_CFG");
-  if (cfg != nullptr) {
+  if (cfg != nullptr && (packed == nullptr || !strstr(cfg, "x1"))) {
     if (!strcmp(cfg, "192x1")) return launch_bt<192, 1>(weight, scales, bias, input, output, m, n, k, ldc, stream);
     if (!strcmp(cfg, "128x1")) return launch_bt<128, 1>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "128x2")) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "160x2")) return launch_bt<160, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "96x2")) return launch_bt<96, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "64x2")) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "32x2")) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "p192")) return launch_pair_bt<192>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-    if (!strcmp(cfg, "p128")) return launch_pair_bt<128>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    if (!strcmp(cfg, "128x2")) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+    if (!strcmp(cfg, "160x2")) return launch_bt<160, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+    if (!strcmp(cfg, "96x2")) return launch_bt<96, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+    if (!strcmp(cfg, "64x2")) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+    if (!strcmp(cfg, "32x2")) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+    if (!strcmp(cfg, "p192")) return launch_pair_bt<192>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+    if (!strcmp(cfg, "p128")) return launch_pair_bt<128>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
   }
   // Short prompts: the smallest token tile that covers them (no padding of
   // the MMA's N to 192).
-  if (m <= 32) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
-  if (m <= 64) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  if (m <= 32) return launch_bt<32, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
+  if (m <= 64) return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
   // 65..128 tokens: two 64-token tiles when the weight tiles alone leave
   // most SMs idle (128 x 896 -> 4864: 10.25 -> 8.62 us).
   if (m <= 128 && (n + kRows - 1) / kRows < 74) {
-    return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    return launch_bt<64, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
   }
-  if (m <= 128) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  if (m <= 128) return launch_bt<128, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
   // Long prompts up to 2^29 outputs: the CTA-pair form, measured 2-6% faster
   // (e.g. 8192 x 4864 -> 896: 92.4 -> 87.3 us); 10% slower at 8192 x 896 ->
   // 151936, which stays on the one-SM form.
   if (m >= 1024 && double(m) * double(n) < double(1 << 29)) {
-    return launch_pair_bt<192>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+    return launch_pair_bt<192>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
   }
-  return launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream);
+  return launch_bt<192, 2>(weight, scales, bias, input, output, m, n, k, ldc, stream, packed);
 }
 
 // BF16 weights in the same transposed form (weights the MMA's M side from
@@ -923,6 +936,50 @@ cudaError_t launch_gemm_w16t(const bf16* weight, const bf16* bias, const bf16* i
   if (m <= 32) return launch_bt<32, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
   if (m <= 64) return launch_bt<64, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
   return launch_bt<128, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
+}
+
+// ---------------------------------------------------------- pre-packing
+// Packed W8A16 weights: [2 ceil(N/256)][ceil(K/128)] tiles of 16 KB; tile
+// (tn, tk) holds rows tn*128.. and K values tk*128.. exactly as the kernels'
+// shared memory holds them after a 128-byte-swizzled TMA load (row r at
+// r * 128, its 16-byte chunk c at position c ^ (r & 7)), zero outside the
+// matrix.  One 1-D bulk copy then brings a tile: contiguous DRAM reads
+// instead of a box of 128 rows x 128 bytes strided by K.
+__global__ void __launch_bounds__(256)
+pack_w8a16_kernel(const int8_t* __restrict__ q, int n, int k, int tiles_k,
+                  uint4* __restrict__ out, size_t chunks) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < chunks;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const size_t tile = i >> 10;  // 1024 chunks of 16 bytes per tile
+    const int within = int(i & 1023);
+    const int r = within >> 3, pos = within & 7;
+    const int c = pos ^ (r & 7);
+    const int tn = int(tile / tiles_k), tk = int(tile % tiles_k);
+    const int row = tn * kRows + r;
+    const int col = tk * 128 + c * 16;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < n && col < k) v = *reinterpret_cast<const uint4*>(q + size_t(row) * k + col);
+    out[i] = v;
+  }
+}
+
+// The tile count along N is rounded up to even: the CTA-pair kernel reads
+// tiles 2 nb and 2 nb + 1 (the padding tiles are zero).
+size_t w8a16_packed_bytes(int n, int k) {
+  if (n <= 0 || k <= 0) return 0;
+  const size_t tiles_n = size_t((n + 2 * kRows - 1) / (2 * kRows)) * 2;
+  return tiles_n * size_t((k + 127) / 128) * 16384;
+}
+
+cudaError_t launch_pack_w8a16(const int8_t* q, int n, int k, void* packed,
+                              cudaStream_t stream) {
+  const size_t chunks = w8a16_packed_bytes(n, k) / 16;
+  if (chunks == 0) return cudaSuccess;
+  size_t grid = (chunks + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  pack_w8a16_kernel<<<unsigned(grid), 256, 0, stream>>>(q, n, k, (k + 127) / 128,
+                                                        static_cast<uint4*>(packed), chunks);
+  return cudaGetLastError();
 }
 
 }  // namespace b200

@@ -48,6 +48,19 @@ def test_invalid_arguments_are_rejected(b200):
     assert A.b200_gemm_bf16(None, None, None, None, 2, 4, -4, None) == -1
     assert A.b200_lm_head_bf16(None, None, None, None, None, None, None, 8, 4, None) == -1
     assert A.b200_argmax_bf16(None, 4, None, None) == -1
+    assert A.b200_gemm_w8a16_packed(None, None, 32, None, None, None, 1, 1, 1, None) == -2
+    assert A.b200_gemm_w8a16_packed(None, None, 64, None, None, None, 2, 4, 16, None) == -1
+    assert A.b200_pack_w8a16(None, 4, 16, None, None) == -1
+    assert A.b200_pack_w8a16(None, 4, 24, None, None) == -1
+
+
+def test_packed_size(b200):
+    A = b200.ABI
+    # [2 ceil(N/256)][ceil(K/128)] blocks of 16 KB
+    assert A.b200_w8a16_packed_bytes(896, 896) == 8 * 7 * 16384
+    assert A.b200_w8a16_packed_bytes(151936, 896) == 1188 * 7 * 16384
+    assert A.b200_w8a16_packed_bytes(128, 4864) == 2 * 38 * 16384
+    assert A.b200_w8a16_packed_bytes(0, 896) == 0
 
 
 def test_empty_shapes_are_noops(b200):
