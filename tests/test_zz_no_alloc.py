@@ -39,7 +39,9 @@ def _run_noalloc(b200, cuda, w, x, vocab, k):
 
 
 @pytest.mark.parametrize("vocab,k,tie", [(151936, 896, (70001, 70002)),
-                                         (1000, 64, (3, 900)), (64, 896, (1, 31))])
+                                         (1000, 64, (3, 900)), (64, 896, (1, 31)),
+                                         (262144, 64, (5, 262143)),  # the stated limit
+                                         (1003, 70, (2, 1002))])     # generic path
 def test_noalloc_matches_workspace_entry_point_twice(b200, oracle, cuda, vocab, k, tie):
     w, x = lm_head_tie_case(vocab, k, *tie) if vocab <= 1000 else (None, None)
     if w is None:
