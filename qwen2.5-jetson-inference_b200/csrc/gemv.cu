@@ -486,13 +486,12 @@ __device__ __forceinline__ float2 ref_bf16_chunks(uint4 w0, uint4 w1, const floa
 }
 
 constexpr int kConsumerWarps = 16;
-constexpr int kBulkThreads = 32 * (kConsumerWarps + 1);
 constexpr int kBulkSmemBudget = 200 * 1024;
 constexpr int kMaxStages = 6;
 
 static __device__ int g_gemv_status = 0;
 
-// Tile geometry.  kWPR == 1: kConsumerWarps warps x (32 / kLPR) row groups
+// Tile geometry.  kWPR == 1: kCW consumer warps x (32 / kLPR) row groups
 // per warp x kR rows per lane group; a row is covered by kLPR lanes (16-byte
 // chunks c = l, l + kLPR, ...), kLPR chosen per shape so that the chunk
 // count divides evenly (896 INT8 = 56 chunks -> 8 lanes); the row groups of
@@ -504,8 +503,9 @@ static __device__ int g_gemv_status = 0;
 // 896): the chunk loop is fully unrolled and every shared-memory offset is
 // an immediate.  kK == 0 handles any in_features.
 // kRef: the reference summation order above (kLPR == 32, kR == 1).
-template <bool kW8, int kLPR, int kR, int kWPR, int kK, bool kRef>
-__global__ void __launch_bounds__(kBulkThreads, 1)
+// kCW: consumer warps (16; 24 for one large-matrix geometry).
+template <bool kW8, int kLPR, int kR, int kWPR, int kK, bool kRef, int kCW = kConsumerWarps>
+__global__ void __launch_bounds__(32 * (kCW + 1), 1)
 gemv_bulk_kernel(const void* __restrict__ weight,
                  const bf16* __restrict__ scales,
                  const bf16* __restrict__ bias,
@@ -520,7 +520,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   constexpr int kGroups = kWPR > 1 ? 1 : 32 / kLPR;  // row groups per warp
   constexpr int kWarpRows = kGroups * kR;
   constexpr int kTileRows =
-      kWPR > 1 ? kConsumerWarps / kWPR : kConsumerWarps * kWarpRows;
+      kWPR > 1 ? kCW / kWPR : kCW * kWarpRows;
   extern __shared__ __align__(128) unsigned char smem_bulk[];
 
   const int warp = threadIdx.x >> 5;
@@ -543,15 +543,15 @@ gemv_bulk_kernel(const void* __restrict__ weight,
   const uint32_t bar_empty = bar_full + 8 * stages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * stages);
   float* red_v = reinterpret_cast<float*>(bars + 2 * stages + 1);
-  int* red_i = reinterpret_cast<int*>(red_v + kConsumerWarps);
-  float* red_part = reinterpret_cast<float*>(red_i + kConsumerWarps);  // [2][warps]
-  float* norm_red = red_part + 2 * kConsumerWarps;                       // [warps]
+  int* red_i = reinterpret_cast<int*>(red_v + kCW);
+  float* red_part = reinterpret_cast<float*>(red_i + kCW);  // [2][warps]
+  float* norm_red = red_part + 2 * kCW;                       // [warps]
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, kConsumerWarps);
+      mbar_init(bar_empty + 8 * s, kCW);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -591,7 +591,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
     if (fusion.in_mode == 1) {
       // RMSNorm of the input: FP32 sum of squares over the consumer threads.
       float ss = 0.0f;
-      for (int e4 = ct; e4 < (k >> 2); e4 += kConsumerWarps * 32) {
+      for (int e4 = ct; e4 < (k >> 2); e4 += kCW * 32) {
         const uint2 raw = reinterpret_cast<const uint2*>(input)[e4];
         const float a = bf16_lo(raw.x), b = bf16_hi(raw.x);
         const float c = bf16_lo(raw.y), d = bf16_hi(raw.y);
@@ -603,14 +603,14 @@ gemv_bulk_kernel(const void* __restrict__ weight,
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       if (lane == 0) norm_red[warp - 1] = ss;
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
       float total = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) total += norm_red[w];
+      for (int w = 0; w < kCW; ++w) total += norm_red[w];
       norm_scale = rsqrtf(total / float(k) + fusion.eps);
     }
     // x -> FP32 planes: xs[p * chunks + c] = x[c*kEPC + 4p .. +3].
-    for (int e4 = ct; e4 < (k >> 2); e4 += kConsumerWarps * 32) {
+    for (int e4 = ct; e4 < (k >> 2); e4 += kCW * 32) {
       const uint2 raw = reinterpret_cast<const uint2*>(input)[e4];
       const int c = (e4 * 4) / kEPC;
       const int p = ((e4 * 4) % kEPC) >> 2;
@@ -631,7 +631,7 @@ gemv_bulk_kernel(const void* __restrict__ weight,
       }
       xs[p * chunks + c] = v;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
 
     const int cw = warp - 1;                  // consumer warp index
     const int gl = lane / kLPR;               // row group within the warp
@@ -745,9 +745,9 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         if constexpr (kWPR > 1) {
           // Partials of the kWPR warps of a row meet in shared memory
           // (double-buffered by tile parity: one barrier per tile).
-          float* part = red_part + (i & 1) * kConsumerWarps;
+          float* part = red_part + (i & 1) * kCW;
           if (lane == 0) part[cw] = v;
-          asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+          asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
           if (ksub == 0) {
             v = 0.0f;
 #pragma unroll
@@ -781,11 +781,11 @@ gemv_bulk_kernel(const void* __restrict__ weight,
         red_v[warp - 1] = best;
         red_i[warp - 1] = best_index;
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
       if (ct == 0) {
         float b = -FLT_MAX;
         int bi = INT_MAX;
-        for (int w = 0; w < kConsumerWarps; ++w) argmax_update(b, bi, red_v[w], red_i[w]);
+        for (int w = 0; w < kCW; ++w) argmax_update(b, bi, red_v[w], red_i[w]);
         block_value[blockIdx.x] = b;
         block_index[blockIdx.x] = bi;
       }
@@ -804,6 +804,7 @@ struct BulkPlan {
   int smem = 0;
   int grid = 0;
   bool ref = false;  // reference summation order (kLPR 32, kR 1)
+  int cw = kConsumerWarps;  // consumer warps per CTA
 };
 
 // SM count of the current device, looked up once per device (a host-side
@@ -853,9 +854,14 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   const int chunks = w8 ? k / 16 : k / 8;
   const int x_bytes = k * 4;
   const int budget = kBulkSmemBudget - x_bytes - 512;
-  struct Cand { int lpr, r, wpr; };
-  const Cand cands[] = {{8, 2, 1}, {8, 1, 1}, {16, 2, 1}, {16, 1, 1}, {32, 4, 1},
-                        {32, 2, 1}, {32, 1, 1}, {32, 1, 2}, {32, 1, 4}};
+  struct Cand { int lpr, r, wpr, cw; };
+  // The last candidate (24 consumer warps, 96-row tiles) serves only large
+  // W8 matrices at in_features 896: 896 -> 151936 in 26.0 vs 27.2 us (more
+  // warps hide the shared-memory load latency); the smaller shapes measured
+  // slower with 24 warps.
+  const Cand cands[] = {{8, 2, 1, 16}, {8, 1, 1, 16}, {16, 2, 1, 16}, {16, 1, 1, 16},
+                        {32, 4, 1, 16}, {32, 2, 1, 16}, {32, 1, 1, 16}, {32, 1, 2, 16},
+                        {32, 1, 4, 16}, {16, 2, 1, 24}};
   // B200_GEMV_PLAN=lpr,r,wpr restricts the choice to that geometry (tuning).
   int force_lpr = 0, force_r = 0, force_wpr = 0;
   if (const char* e = getenv("B200_GEMV_PLAN")) {
@@ -863,9 +869,12 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
   }
   for (const Cand& c : cands) {
     if (force_lpr > 0 && (c.lpr != force_lpr || c.r != force_r || c.wpr != force_wpr)) continue;
-    const int rows = c.wpr > 1 ? kConsumerWarps / c.wpr
-                               : kConsumerWarps * (32 / c.lpr) * c.r;
+    if (c.cw != kConsumerWarps && !(w8 && k == 896 && n >= 16384)) continue;
+    const int rows = c.wpr > 1 ? c.cw / c.wpr : c.cw * (32 / c.lpr) * c.r;
     if (rows < min_rows) continue;
+    // Each tile's scale rows are one 1-D bulk copy: its source offset
+    // (row0 * groups * 2 bytes) must stay 16-byte aligned.
+    if (w8 && (rows * groups * 2) % 16 != 0) continue;
     const int wt = rows * row_bytes;
     const int st = (wt + (w8 ? rows * groups * 2 : 0) + 127) / 128 * 128;
     const int stages = budget / st < kMaxStages ? budget / st : kMaxStages;
@@ -891,8 +900,8 @@ BulkPlan plan_bulk(bool w8, int n, int k, int min_rows) {
       best.stages = stages;
       best.stage_bytes = st;
       best.w_tile_bytes = wt;
-      best.smem = stages * st + x_bytes + 8 * 2 * stages + 8 +
-                  8 * kConsumerWarps + 8 * kConsumerWarps + 4 * kConsumerWarps;
+      best.smem = stages * st + x_bytes + 8 * 2 * stages + 8 + 8 * c.cw + 8 * c.cw + 4 * c.cw;
+      best.cw = c.cw;
       best.grid = tiles < sms ? tiles : sms;
     }
   }
@@ -913,6 +922,9 @@ BulkPlan plan_bulk_ref(bool w8, int n, int k, bool lm_head) {
   const int st = (rows * row_bytes + (w8 ? rows * groups * 2 : 0) + 127) / 128 * 128;
   const int stages = budget / st < 16 ? budget / st : 16;
   if (stages < 2) return p;
+  // 16-byte aligned scale copies per tile (4-row tiles need an even group
+  // count); otherwise no reference-order plan (the call takes the fast one).
+  if (w8 && (rows * groups * 2) % 16 != 0) return p;
   const int tiles = (n + rows - 1) / rows;
   int grid = tiles < sms ? tiles : sms;
   if (lm_head && grid > (n + 7) / 8) grid = (n + 7) / 8;  // ceil(n/8) partials
@@ -929,19 +941,20 @@ BulkPlan plan_bulk_ref(bool w8, int n, int k, bool lm_head) {
   return p;
 }
 
-template <bool kW8, int kLPR, int kR, int kWPR, bool kRef = false>
+template <bool kW8, int kLPR, int kR, int kWPR, bool kRef = false, int kCW = kConsumerWarps>
 cudaError_t launch_bulk(const BulkPlan& p, const void* w, const bf16* s,
                         const bf16* b, const bf16* x, bf16* y, int n, int k,
                         float* bv, int* bi, cudaStream_t stream,
                         const GemvFusion& fusion) {
-  auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef>
-                         : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef>;
-  cudaError_t e = k == 896 ? bulk_smem_attr<gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef>>()
-                           : bulk_smem_attr<gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef>>();
+  auto kernel = k == 896 ? gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef, kCW>
+                         : gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef, kCW>;
+  cudaError_t e = k == 896
+                      ? bulk_smem_attr<gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 896, kRef, kCW>>()
+                      : bulk_smem_attr<gemv_bulk_kernel<kW8, kLPR, kR, kWPR, 0, kRef, kCW>>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
-  cfg.blockDim = dim3(kBulkThreads);
+  cfg.blockDim = dim3(32 * (kCW + 1));
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -961,6 +974,9 @@ cudaError_t dispatch_bulk(const BulkPlan& p, const void* w, const bf16* s,
     return p.wpr == 4
                ? launch_bulk<kW8, 32, 1, 4, true>(p, w, s, b, x, y, n, k, bv, bi, st, f)
                : launch_bulk<kW8, 32, 1, 1, true>(p, w, s, b, x, y, n, k, bv, bi, st, f);
+  }
+  if constexpr (kW8) {
+    if (p.cw == 24) return launch_bulk<true, 16, 2, 1, false, 24>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   }
   if (p.wpr == 4) return launch_bulk<kW8, 32, 1, 4>(p, w, s, b, x, y, n, k, bv, bi, st, f);
   if (p.wpr == 2) return launch_bulk<kW8, 32, 1, 2>(p, w, s, b, x, y, n, k, bv, bi, st, f);
