@@ -1382,6 +1382,13 @@ cudaError_t reserve_gemm_scratch(size_t bytes) {
 
 // Prompts of < 1024 tokens on the TMEM-weight kernel unless
 // B200_GEMM_W8T_SHORT=0 (read at every call, for measurement).
+// Cluster split-K for short prompts on narrow matrices unless
+// B200_GEMM_CSPLIT=0 (read at every call).
+static bool use_cluster_split() {
+  const char* e = getenv("B200_GEMM_CSPLIT");
+  return e == nullptr || strcmp(e, "0") != 0;
+}
+
 static bool use_w16t(int m, int n, int k) {
   const char* e = getenv("B200_GEMM_W16T");
   if (e != nullptr) return strcmp(e, "1") == 0;
@@ -1397,6 +1404,12 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
+  if (peers.n == 0 && m <= kSplitMaxTokens && summation_order() == B200_ORDER_FAST &&
+      use_cluster_split() && gemm_w8t_supported(weight, input, output, m, n, k)) {
+    const cudaError_t e = launch_gemm_cluster_split(w8, weight, scales, bias, input, output,
+                                                    m, n, k, ldc, stream);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (peers.n == 0 && m <= kSplitMaxTokens) {
     const cudaError_t e =
         gemm_split_k(w8, weight, scales, bias, input, output, m, n, k, ldc, stream);

@@ -879,6 +879,333 @@ cudaError_t launch_pair_bt(const void* weight, const bf16* scales, const bf16* b
                             ldc, static_cast<const unsigned char*>(packed));
 }
 
+// ===================================================================
+// Short prompts, few weight tiles: K split across a thread-block cluster.
+//
+// With <= 128 tokens and a narrow matrix (896 or 1152 outputs: 7-9 weight
+// tiles) the kernels above keep only 7-9 SMs busy, each walking all of K.
+// Here a cluster of S CTAs (S <= 8) shares one weight tile: CTA r of the
+// cluster runs k-blocks [r*nkb/S, (r+1)*nkb/S) through the same
+// TMA -> dequantise -> TMEM -> tcgen05.mma pipeline (single tile, single
+// accumulator), parks its FP32 partial D [kBT tokens x 128 features] in its
+// own shared memory, and after a cluster barrier CTA r adds, for its slice
+// of the tokens, the S partials in rank order 0..S-1 read through
+// distributed shared memory (ld.shared::cluster), then adds the bias and
+// stores BF16.  One launch, no global scratch, deterministic; a different
+// FP32 summation order from the unsplit kernels (fast order only).
+// Every wait is bounded (2 s).
+// ===================================================================
+template <int kBT, bool kW16>
+struct CfgS {
+  static constexpr int kSub = 2;
+  static constexpr int kKS = kBK * kSub;                  // K per stage
+  static constexpr int kDqWarps = kW16 ? 0 : 8;
+  static constexpr int kXSub = kBT * kBK * 2;
+  static constexpr int kXBytes = kSub * kXSub;
+  static constexpr int kWSub = kRows * kBK * 2;
+  static constexpr int kQBytes = kW16 ? kSub * kWSub : kRows * kKS;
+  static constexpr int kStageBytes = kXBytes + kQBytes;
+  static constexpr int kRedBytes = kBT * kRows * 4;       // FP32 partial [tok][feat]
+  static constexpr int kStages = 3 * kStageBytes + kRedBytes <= 216 * 1024 ? 3 : 2;
+  static constexpr int kACols = kKS / 2;
+  static constexpr int kAStages = kW16 ? 1 : 2;
+  static constexpr int kACol0 = kBT;
+  static constexpr int kTmemCols = 256;                   // kBT + 2 x 64 <= 256
+  static constexpr int kThreads = (8 + kDqWarps) * 32;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kRedBytes + 512 + 1024;
+  static_assert(kBT == 32 || kBT == 64 || kBT == 128, "token tile");
+  static_assert(kW16 || kBT + kAStages * kACols <= kTmemCols, "TMEM columns");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+template <int kBT, bool kW16>
+__global__ void __launch_bounds__(CfgS<kBT, kW16>::kThreads, 1)
+gemm_w8t_split_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                      const __grid_constant__ CUtensorMap tmap_q,
+                      const uint16_t* __restrict__ scales, const bf16* __restrict__ bias,
+                      bf16* __restrict__ out, int m, int n, int k, int ldc) {
+  using C = CfgS<kBT, kW16>;
+  extern __shared__ __align__(1024) unsigned char smem_raws[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raws) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(red) +
+                                               C::kRedBytes);
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_empty = bar_full + 8 * C::kStages;
+  const uint32_t bar_afull = bar_empty + 8 * C::kStages;
+  const uint32_t bar_aempty = bar_afull + 8 * C::kAStages;
+  const uint32_t bar_acc = bar_aempty + 8 * C::kAStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 2 * C::kAStages + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int splits = int(gridDim.x);          // = cluster size
+  const int rank = int(cluster_ctarank());
+  const int nb = int(blockIdx.y), mb = int(blockIdx.z);
+  const int num_kb = (k + C::kKS - 1) / C::kKS;
+  const int kb0 = rank * num_kb / splits, kb1 = (rank + 1) * num_kb / splits;
+  const int groups = (k + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1 + C::kDqWarps);
+    }
+    for (int a = 0; a < C::kAStages; ++a) {
+      mbar_init(bar_afull + 8 * a, C::kDqWarps > 0 ? C::kDqWarps : 1);
+      mbar_init(bar_aempty + 8 * a, 1);
+    }
+    mbar_init(bar_acc, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait_primary();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait_t(bar_empty + 8 * stage, phase ^ 1, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE))
+          break;
+        unsigned char* st = smem + stage * C::kStageBytes;
+        const uint32_t fb = bar_full + 8 * stage;
+        mbar_arrive_expect_tx(fb, C::kStageBytes);
+#pragma unroll
+        for (int sub = 0; sub < C::kSub; ++sub) {
+          tma_load_2d(smem_u32(st + sub * C::kXSub), &tmap_x, kb * C::kKS + sub * kBK,
+                      mb * kBT, fb);
+          if constexpr (kW16) {
+            tma_load_2d(smem_u32(st + C::kXBytes + sub * C::kWSub), &tmap_q,
+                        kb * C::kKS + sub * kBK, nb * kRows, fb);
+          }
+        }
+        if constexpr (!kW16) {
+          tma_load_2d(smem_u32(st + C::kXBytes), &tmap_q, kb * C::kKS, nb * kRows, fb);
+        }
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, kBT);
+      int stage = 0, aslot = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait_t(kW16 ? bar_full + 8 * stage : bar_afull + 8 * aslot, kW16 ? phase : aphase,
+                    abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t x_addr = smem_u32(smem + stage * C::kStageBytes);
+        const uint32_t acc = (kb > kb0) ? 1u : 0u;
+        if constexpr (kW16) {
+          const uint32_t w_addr = x_addr + C::kXBytes;
+#pragma unroll
+          for (int kk = 0; kk < C::kKS / 16; ++kk) {
+            mma_bf16(tmem_base, desc_sw128(w_addr + (kk >> 2) * C::kWSub + (kk & 3) * 32),
+                     desc_sw128(x_addr + (kk >> 2) * C::kXSub + (kk & 3) * 32), idesc,
+                     (acc || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar_empty + 8 * stage);
+        } else {
+          const uint32_t a_addr = tmem_base + uint32_t(C::kACol0 + aslot * C::kACols);
+#pragma unroll
+          for (int kk = 0; kk < C::kKS / 16; ++kk) {
+            mma_bf16_ta(tmem_base, a_addr + uint32_t(kk * 8),
+                        desc_sw128(x_addr + (kk >> 2) * C::kXSub + (kk & 3) * 32), idesc,
+                        (acc || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar_empty + 8 * stage);
+          mma_commit(bar_aempty + 8 * aslot);
+        }
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++aslot == C::kAStages) {
+          aslot = 0;
+          aphase ^= 1;
+        }
+      }
+      if (ok) mma_commit(bar_acc);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------- partial D -> this CTA's shared memory [tok][feat]
+    const int q = warp & 3;
+    const bool ok = __all_sync(0xffffffffu,
+                               wait_t(bar_acc, 0, abort_flag, B200_DEVICE_TIMEOUT_ACCUM));
+    tc_fence_after();
+#pragma unroll 1
+    for (int c0 = 0; c0 < kBT; c0 += 16) {
+      uint32_t r[16];
+      if (ok) {
+        tmem_ld16(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(c0), r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) red[(c0 + j) * kRows + q * 32 + lane] = __uint_as_float(r[j]);
+    }
+    tc_fence_before();
+  } else if (!kW16 && warp >= 8) {
+    // ---------------------------------------------------------- dequantiser
+    const int dw = warp - 8;
+    const int quarter = dw & 3;
+    const int part = dw >> 2;
+    const int rl = quarter * 32 + lane;
+    const uint32_t t_lane = uint32_t(quarter * 32) << 16;
+    const int sw = rl & 7;
+    constexpr int kChunks = 4;
+    const int row = nb * kRows + rl;
+    const bool srow_ok = row < n;
+    const uint16_t* srow = scales + size_t(srow_ok ? row : 0) * groups;
+    int stage = 0, aslot = 0;
+    uint32_t phase = 0, aphase = 0;
+    for (int kb = kb0; kb < kb1; ++kb) {
+      const int g = kb * 2 + part;
+      const uint32_t sv = (srow_ok && g < groups) ? uint32_t(srow[g]) : 0u;
+      if (!wait_t(bar_full + 8 * stage, phase, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE)) break;
+      const unsigned char* qt = smem + stage * C::kStageBytes + C::kXBytes + rl * C::kKS;
+      uint4 c[kChunks];
+#pragma unroll
+      for (int j = 0; j < kChunks; ++j) {
+        c[j] = *reinterpret_cast<const uint4*>(qt + (((part * kChunks + j) ^ sw) << 4));
+      }
+      const uint32_t s2bits = sv | (sv << 16);
+      const bf162 s2 = *reinterpret_cast<const bf162*>(&s2bits);
+      uint32_t v[8 * kChunks];
+#pragma unroll
+      for (int j = 0; j < kChunks; ++j) {
+        dq4(c[j].x, s2, v + 8 * j + 0);
+        dq4(c[j].y, s2, v + 8 * j + 2);
+        dq4(c[j].z, s2, v + 8 * j + 4);
+        dq4(c[j].w, s2, v + 8 * j + 6);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
+      if (!wait_t(bar_aempty + 8 * aslot, aphase ^ 1, abort_flag, B200_DEVICE_TIMEOUT_PIPELINE))
+        break;
+      tc_fence_after();
+      const uint32_t ta = tmem_base + t_lane +
+                          uint32_t(C::kACol0 + aslot * C::kACols + part * (C::kACols / 2));
+#pragma unroll
+      for (int j = 0; j < kChunks / 2; ++j) tmem_st16(ta + 16 * j, v + 16 * j);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_afull + 8 * aslot);
+      if (++stage == C::kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+      if (++aslot == C::kAStages) {
+        aslot = 0;
+        aphase ^= 1;
+      }
+    }
+  }
+
+  // ------------------------------ fixed-order reduction across the cluster
+  cluster_sync_all();  // every CTA's partial is in its shared memory
+  {
+    const int t0 = rank * kBT / splits, t1 = (rank + 1) * kBT / splits;
+    const uint32_t red_local = smem_u32(red);
+    for (int idx = int(threadIdx.x); idx < (t1 - t0) * kRows; idx += C::kThreads) {
+      const int t = t0 + idx / kRows, f = idx % kRows;
+      const uint32_t off = uint32_t((t * kRows + f) * 4);
+      float sum = 0.0f;
+      for (int j = 0; j < splits; ++j) {
+        float v;
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(v)
+                     : "r"(map_to_rank(red_local, uint32_t(j)) + off)
+                     : "memory");
+        sum += v;
+      }
+      const int feat = nb * kRows + f, tok = mb * kBT + t;
+      if (tok < m && feat < n) {
+        if (bias != nullptr) sum += __bfloat162float(bias[feat]);
+        out[size_t(tok) * ldc + feat] = __float2bfloat16_rn(sum);
+      }
+    }
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its partial
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(C::kTmemCols)
+                 : "memory");
+  }
+}
+
+template <int kBT, bool kW16>
+cudaError_t launch_split_bt(const void* weight, const bf16* scales, const bf16* bias,
+                            const bf16* input, bf16* output, int m, int n, int k, int ldc,
+                            int splits, cudaStream_t stream) {
+  using C = CfgS<kBT, kW16>;
+  CUtensorMap tx, tq;
+  if (!encode_tmap_2d(&tx, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, m, kBK, kBT,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !(kW16 ? encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, n, kBK,
+                              kRows, CU_TENSOR_MAP_SWIZZLE_128B)
+             : encode_tmap_2d(&tq, weight, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, C::kKS,
+                              kRows, CU_TENSOR_MAP_SWIZZLE_128B))) {
+    return cudaErrorInvalidValue;
+  }
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? 1ull << dev : 0ull;
+  if (bit == 0 || (attr_done.load(std::memory_order_acquire) & bit) == 0) {
+    const cudaError_t e = cudaFuncSetAttribute(gemm_w8t_split_kernel<kBT, kW16>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(bit, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits, (n + kRows - 1) / kRows, (m + kBT - 1) / kBT);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gemm_w8t_split_kernel<kBT, kW16>, tx, tq,
+                            reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k,
+                            ldc);
+}
+
 }  // namespace
 
 bool gemm_w8t_supported(const void* weight, const void* input, const void* output, int m,
@@ -936,6 +1263,41 @@ cudaError_t launch_gemm_w16t(const bf16* weight, const bf16* bias, const bf16* i
   if (m <= 32) return launch_bt<32, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
   if (m <= 64) return launch_bt<64, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
   return launch_bt<128, 2, true>(weight, nullptr, bias, input, output, m, n, k, ldc, stream);
+}
+
+// Cluster split-K for short prompts on narrow matrices (fast order).
+// Returns cudaErrorNotSupported when the shape does not qualify: <= 128
+// tokens, at most 37 output tiles (a quarter of the SMs), at least two
+// 128-wide k-blocks per split, and a shape where it measured faster: long K
+// (32 x 4864 -> 896: W8A16 25.8 -> 7.3 us, BF16 18.5 -> 6.0 us; 128 tokens:
+// 26.5 -> 9.7 / 21.0 -> 9.8 us, ahead of the reserved-buffer split) or
+// W8A16 at <= 32 tokens (896 -> 896: 7.5 -> 6.3 us).  At K = 896 with more
+// tokens, or in BF16, the unsplit kernels stay faster.
+cudaError_t launch_gemm_cluster_split(bool w8, const void* weight, const bf16* scales,
+                                      const bf16* bias, const bf16* input, bf16* output,
+                                      int m, int n, int k, int ldc, cudaStream_t stream) {
+  if (m <= 0 || m > 128) return cudaErrorNotSupported;
+  if (!(k >= 2048 || (w8 && m <= 32))) return cudaErrorNotSupported;
+  const int bt = m <= 32 ? 32 : (m <= 64 ? 64 : 128);
+  const int tiles = ((n + kRows - 1) / kRows) * ((m + bt - 1) / bt);
+  const int num_kb = (k + 127) / 128;
+  if (tiles > 37) return cudaErrorNotSupported;
+  int sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int splits = sms / tiles;
+  if (splits > 8) splits = 8;
+  if (splits > num_kb / 2) splits = num_kb / 2;
+  if (splits < 2) return cudaErrorNotSupported;
+  if (w8) {
+    if (bt == 32) return launch_split_bt<32, false>(weight, scales, bias, input, output, m, n, k, ldc, splits, stream);
+    if (bt == 64) return launch_split_bt<64, false>(weight, scales, bias, input, output, m, n, k, ldc, splits, stream);
+    return launch_split_bt<128, false>(weight, scales, bias, input, output, m, n, k, ldc, splits, stream);
+  }
+  if (bt == 32) return launch_split_bt<32, true>(weight, nullptr, bias, input, output, m, n, k, ldc, splits, stream);
+  if (bt == 64) return launch_split_bt<64, true>(weight, nullptr, bias, input, output, m, n, k, ldc, splits, stream);
+  return launch_split_bt<128, true>(weight, nullptr, bias, input, output, m, n, k, ldc, splits, stream);
 }
 
 // ---------------------------------------------------------- pre-packing

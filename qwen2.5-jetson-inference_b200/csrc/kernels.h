@@ -100,6 +100,12 @@ cudaError_t launch_gemm_w8t(const void* weight, const bf16* scales, const bf16* 
 // Pre-packed W8A16 weights (tile-major 16 KB blocks in the kernels'
 // shared-memory layout); `packed` given to launch_gemm_w8t replaces the
 // strided TMA weight loads by 1-D bulk copies.
+// K split across a thread-block cluster with a fixed-order reduction in
+// distributed shared memory (fast summation order; cudaErrorNotSupported for
+// shapes it does not take).
+cudaError_t launch_gemm_cluster_split(bool w8, const void* weight, const bf16* scales,
+                                      const bf16* bias, const bf16* input, bf16* output,
+                                      int m, int n, int k, int ldc, cudaStream_t stream);
 size_t w8a16_packed_bytes(int n, int k);
 cudaError_t launch_pack_w8a16(const int8_t* q, int n, int k, void* packed, cudaStream_t stream);
 // The same transposed form with BF16 weights read by the MMA from shared

@@ -41,7 +41,22 @@ def test_engine_matches_reference_engine(mods, oracle, precision, mode, tmp_path
     assert cos >= 0.9999, cos
     toks, ttft, dec = e.generate(prompt, 48)
     same = next((i for i, (a, b) in enumerate(zip(toks, ref["tokens"])) if a != b), 48)
-    assert same >= 16, (same, toks[:20], ref["tokens"][:20])
+    if same < 16:
+        # The fast summation order promises agreement within rounding, not
+        # identity (the reference order does, tests/test_e2e_gpu.py): an early
+        # divergence must sit at a near tie.  Forced along the reference's
+        # tokens up to it, the engine's logit for the reference's token is
+        # within one BF16 ulp of its own largest.
+        import ctypes
+        arr = (ctypes.c_int * len(prompt))(*prompt)
+        assert eng.ABI.b200_engine_prefill(e.handle, arr, len(prompt)) == 0
+        for t in ref["tokens"][:same]:
+            assert eng.ABI.b200_engine_force_token(e.handle, int(t)) == 0
+            assert eng.ABI.b200_engine_decode(e.handle, 1) == 0
+        v = oracle.bf16_to_f32(e.logits())
+        top = float(v.max())
+        gap = top - float(v[ref["tokens"][same]])
+        assert gap <= abs(top) * 2.0 ** -7 * 1.01, (same, gap, top)
     assert e.device_status() == 0
     e.close()
 

@@ -221,13 +221,17 @@ def test_short_prompt_split_k(b200, oracle, cuda, m, k, n, w8):
         def call(y):
             b200.gemm_bf16(dw, db, dx, y, m, n, k)
     ys = [torch.empty(m, n, dtype=torch.bfloat16, device=cuda) for _ in range(3)]
-    call(ys[0])
-    call(ys[1])
-    os.environ["B200_GEMM_NO_SPLITK"] = "1"
+    # the cluster split (which takes these shapes first) off: this test
+    # covers the reserved-buffer split
+    os.environ["B200_GEMM_CSPLIT"] = "0"
     try:
+        call(ys[0])
+        call(ys[1])
+        os.environ["B200_GEMM_NO_SPLITK"] = "1"
         call(ys[2])
     finally:
-        del os.environ["B200_GEMM_NO_SPLITK"]
+        os.environ.pop("B200_GEMM_NO_SPLITK", None)
+        del os.environ["B200_GEMM_CSPLIT"]
     torch.cuda.synchronize()
     assert torch.equal(ys[0], ys[1])
     got = oracle.bf16_to_f32(to_bits(ys[0]))
@@ -327,10 +331,12 @@ def test_w8a16_packed_weights_bit_identical(b200, oracle, cuda, m, k, n):
     y1 = torch.empty_like(y0)
     import os
     os.environ["B200_GEMM_NO_SPLITK"] = "1"  # same kernel as the packed call
+    os.environ["B200_GEMM_CSPLIT"] = "0"
     try:
         b200.gemm_w8a16(q, s, 64, bias, x, y0, m, n, k)
     finally:
         del os.environ["B200_GEMM_NO_SPLITK"]
+        del os.environ["B200_GEMM_CSPLIT"]
     b200.gemm_w8a16_packed(packed, s, 64, bias, x, y1, m, n, k)
     torch.cuda.synchronize()
     assert b200.device_status() == 0
@@ -359,3 +365,52 @@ def test_w8a16_packed_weights_bit_identical(b200, oracle, cuda, m, k, n):
                     col = kt * 128 + c * 16
                     exp = qn[row, col:col + 16] if row < n and col < k else np.zeros(16, np.uint8)
                     assert np.array_equal(blk[r, c ^ (r & 7)], exp)
+
+
+@pytest.mark.parametrize("m,k,n", [(32, 896, 896), (32, 4864, 896), (128, 4864, 896),
+                                   (7, 2112, 264), (100, 2176, 1000), (17, 896, 128)])
+@pytest.mark.parametrize("w8", [True, False], ids=["w8a16", "bf16"])
+def test_cluster_split_k(b200, oracle, cuda, m, k, n, w8):
+    """Short prompts on narrow matrices in the fast order: K split across a
+    thread-block cluster, partials summed in rank order through distributed
+    shared memory.  Every row against the oracle; two runs bit-identical; the
+    unsplit kernels (B200_GEMM_CSPLIT=0, no reserved K split) within one BF16
+    ulp on the same inputs."""
+    import os
+    import torch
+    rng = np.random.default_rng(m * 13 + k + n)
+    w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+    bb = oracle.f32_to_bf16(rng.normal(0, 0.02, n).astype(np.float32))
+    xb = oracle.f32_to_bf16(rng.standard_normal((m, k)).astype(np.float32))
+    dx, db = from_bits(xb, cuda), from_bits(bb, cuda)
+    if w8:
+        q, sb = oracle.quantize_groupwise(w)
+        dq, ds = torch.from_numpy(q).to(cuda), from_bits(sb, cuda)
+        exp = oracle.bf16_to_f32(oracle.linear_w8a16(q, sb, bb, xb, gemm=True))
+
+        def call(y):
+            b200.gemm_w8a16(dq, ds, 64, db, dx, y, m, n, k)
+    else:
+        wb = oracle.f32_to_bf16(w)
+        dw = from_bits(wb, cuda)
+        exp = oracle.bf16_to_f32(oracle.f32_to_bf16(oracle.linear_bf16(wb, bb, xb)))
+
+        def call(y):
+            b200.gemm_bf16(dw, db, dx, y, m, n, k)
+    ys = [torch.empty(m, n, dtype=torch.bfloat16, device=cuda) for _ in range(3)]
+    call(ys[0])
+    call(ys[1])
+    os.environ["B200_GEMM_CSPLIT"] = "0"
+    os.environ["B200_GEMM_NO_SPLITK"] = "1"
+    try:
+        call(ys[2])
+    finally:
+        del os.environ["B200_GEMM_CSPLIT"]
+        del os.environ["B200_GEMM_NO_SPLITK"]
+    torch.cuda.synchronize()
+    assert b200.device_status() == 0
+    assert torch.equal(ys[0], ys[1])
+    got = oracle.bf16_to_f32(to_bits(ys[0]))
+    assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
+    unsplit = oracle.bf16_to_f32(to_bits(ys[2]))
+    assert np.all(np.abs(got - unsplit) <= np.abs(unsplit) * 2.0 ** -7 * 1.01 + 1e-4)
