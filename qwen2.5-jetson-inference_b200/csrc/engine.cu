@@ -120,6 +120,36 @@ __global__ void rmsnorm_rows_kernel(const bf16* __restrict__ in, const bf16* __r
 }
 
 // x = bf16(x + r), elementwise.
+// x[row] = bf16(x[row] + r[row]), then out[row] = RMSNorm of the stored
+// row (same roundings as add_kernel followed by rmsnorm_rows_kernel, one
+// launch instead of two).
+__global__ void add_rmsnorm_rows_kernel(bf16* __restrict__ x, const bf16* __restrict__ r,
+                                        const bf16* __restrict__ w, bf16* __restrict__ out,
+                                        int hidden, float eps) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  bf16* row = x + size_t(blockIdx.x) * hidden;
+  const bf16* rrow = r + size_t(blockIdx.x) * hidden;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const bf16 s = __float2bfloat16_rn(__bfloat162float(row[i]) + __bfloat162float(rrow[i]));
+    row[i] = s;
+    const float v = __bfloat162float(s);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.0f;
+  for (int i = 0; i < int(blockDim.x >> 5); ++i) total += red[i];
+  const float scale = rsqrtf(total / float(hidden) + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    out[size_t(blockIdx.x) * hidden + i] = __float2bfloat16_rn(
+        __bfloat162float(row[i]) * __bfloat162float(w[i]) * scale);
+  }
+}
 __global__ void add_kernel(bf16* __restrict__ x, const bf16* __restrict__ r, size_t n) {
   pdl_launch_dependents();
   pdl_wait_primary();
@@ -309,8 +339,12 @@ int layer_forward(b200_engine* e, int l, int t_rows, bool decode) {
     ENGINE_TRY(check(b200::launch_gemv(w8, L.qkv_w, B(L.qkv_s), B(L.qkv_b), e->x, e->qkv,
                                        e->qkv_dim, H, nullptr, nullptr, s, nullptr, &f)));
   } else {
-    ENGINE_TRY(launch(b200::rmsnorm_rows_kernel, dim3(t_rows), dim3(256), 0, s,
-                      (const bf16*)e->x, B(L.input_norm), e->xn, H, c.eps));
+    // Layers after the first receive xn = RMSNorm(x) from the previous
+    // layer's fused residual add.
+    if (l == 0) {
+      ENGINE_TRY(launch(b200::rmsnorm_rows_kernel, dim3(t_rows), dim3(256), 0, s,
+                        (const bf16*)e->x, B(L.input_norm), e->xn, H, c.eps));
+    }
     ENGINE_TRY(w8 ? b200_gemm_w8a16(static_cast<const int8_t*>(L.qkv_w), L.qkv_s, 64, L.qkv_b,
                                     reinterpret_cast<const uint16_t*>(e->xn),
                                     reinterpret_cast<uint16_t*>(e->qkv), t_rows, e->qkv_dim, H, s)
@@ -359,16 +393,20 @@ int layer_forward(b200_engine* e, int l, int t_rows, bool decode) {
   };
   const size_t th = size_t(t_rows) * H;
   ENGINE_TRY(gemm(L.o_w, L.o_s, e->att, e->tmp, H, H));
-  ENGINE_TRY(launch(b200::add_kernel, dim3(b200::grid_for(th)), dim3(256), 0, s, e->x,
-                    (const bf16*)e->tmp, th));
-  ENGINE_TRY(launch(b200::rmsnorm_rows_kernel, dim3(t_rows), dim3(256), 0, s,
-                    (const bf16*)e->x, B(L.post_norm), e->xn, H, c.eps));
+  ENGINE_TRY(launch(b200::add_rmsnorm_rows_kernel, dim3(t_rows), dim3(256), 0, s, e->x,
+                    (const bf16*)e->tmp, B(L.post_norm), e->xn, H, c.eps));
   ENGINE_TRY(gemm(L.gate_up_w, L.gate_up_s, e->xn, e->gu, 2 * I, H));
   ENGINE_TRY(launch(b200::silu_mul_kernel, dim3(b200::grid_for(size_t(t_rows) * I)), dim3(256),
                     0, s, (const bf16*)e->gu, e->h, t_rows, I));
   ENGINE_TRY(gemm(L.down_w, L.down_s, e->h, e->tmp, H, I));
-  ENGINE_TRY(launch(b200::add_kernel, dim3(b200::grid_for(th)), dim3(256), 0, s, e->x,
-                    (const bf16*)e->tmp, th));
+  if (l + 1 < c.layers) {
+    // Residual add fused with the next layer's input RMSNorm.
+    ENGINE_TRY(launch(b200::add_rmsnorm_rows_kernel, dim3(t_rows), dim3(256), 0, s, e->x,
+                      (const bf16*)e->tmp, B(e->layers[l + 1].input_norm), e->xn, H, c.eps));
+  } else {
+    ENGINE_TRY(launch(b200::add_kernel, dim3(b200::grid_for(th)), dim3(256), 0, s, e->x,
+                      (const bf16*)e->tmp, th));
+  }
   return B200_OK;
 }
 
