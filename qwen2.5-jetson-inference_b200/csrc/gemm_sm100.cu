@@ -1404,7 +1404,7 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
                                  const bf16* bias, const bf16* input, bf16* output,
                                  int m, int n, int k, int ldc, const PeerOuts& peers,
                                  cudaStream_t stream) {
-  if (peers.n == 0 && m <= kSplitMaxTokens && summation_order() == B200_ORDER_FAST &&
+  if (peers.n == 0 && m <= 512 && summation_order() == B200_ORDER_FAST &&
       use_cluster_split() && gemm_w8t_supported(weight, input, output, m, n, k)) {
     const cudaError_t e = launch_gemm_cluster_split(w8, weight, scales, bias, input, output,
                                                     m, n, k, ldc, stream);

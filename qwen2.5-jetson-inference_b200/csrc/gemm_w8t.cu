@@ -1266,8 +1266,8 @@ cudaError_t launch_gemm_w16t(const bf16* weight, const bf16* bias, const bf16* i
 }
 
 // Cluster split-K for short prompts on narrow matrices (fast order).
-// Returns cudaErrorNotSupported when the shape does not qualify: <= 128
-// tokens, at most 37 output tiles (a quarter of the SMs), at least two
+// Returns cudaErrorNotSupported when the shape does not qualify: <= 512
+// tokens (<= 128 unless K is long), at most 37 output tiles (a quarter of the SMs), at least two
 // 128-wide k-blocks per split, and a shape where it measured faster: long K
 // (32 x 4864 -> 896: W8A16 25.8 -> 7.3 us, BF16 18.5 -> 6.0 us; 128 tokens:
 // 26.5 -> 9.7 / 21.0 -> 9.8 us, ahead of the reserved-buffer split) or
@@ -1276,12 +1276,19 @@ cudaError_t launch_gemm_w16t(const bf16* weight, const bf16* bias, const bf16* i
 cudaError_t launch_gemm_cluster_split(bool w8, const void* weight, const bf16* scales,
                                       const bf16* bias, const bf16* input, bf16* output,
                                       int m, int n, int k, int ldc, cudaStream_t stream) {
-  if (m <= 0 || m > 128) return cudaErrorNotSupported;
+  if (m <= 0 || m > 512) return cudaErrorNotSupported;
   if (!(k >= 2048 || (w8 && m <= 32))) return cudaErrorNotSupported;
   const int bt = m <= 32 ? 32 : (m <= 64 ? 64 : 128);
   const int tiles = ((n + kRows - 1) / kRows) * ((m + bt - 1) / bt);
   const int num_kb = (k + 127) / 128;
   if (tiles > 37) return cudaErrorNotSupported;
+  // 129..512 tokens (measured): long K with room for ~8 splits (256 x 4864 ->
+  // 896: 31.0 -> 10.2 us; 512 x 4864 -> 128: 30.8 -> 9.5 us), or W8A16 with
+  // K >= 4096 (512 x 4864 -> 896: 31.2 -> 24.1 us); fewer splits or K = 2048
+  // measured slower.
+  if (m > 128 && !(k >= 2048 && (tiles <= 18 || (w8 && k >= 4096)))) {
+    return cudaErrorNotSupported;
+  }
   int sms = 148;
   int dev = 0;
   cudaGetDevice(&dev);

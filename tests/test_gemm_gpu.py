@@ -368,7 +368,8 @@ def test_w8a16_packed_weights_bit_identical(b200, oracle, cuda, m, k, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(32, 896, 896), (32, 4864, 896), (128, 4864, 896),
-                                   (7, 2112, 264), (100, 2176, 1000), (17, 896, 128)])
+                                   (7, 2112, 264), (100, 2176, 1000), (17, 896, 128),
+                                   (256, 4864, 896), (300, 4864, 264), (512, 4864, 896)])
 @pytest.mark.parametrize("w8", [True, False], ids=["w8a16", "bf16"])
 def test_cluster_split_k(b200, oracle, cuda, m, k, n, w8):
     """Short prompts on narrow matrices in the fast order: K split across a
