@@ -1432,7 +1432,14 @@ cudaError_t launch_gemm_tc_peers(bool w8, const void* weight, const bf16* scales
   // than the shared-memory dequant kernel at 32, 128 and 512 tokens, 2x on
   // 896 -> 151936); its epilogue has no peer stores, so the sharded form
   // keeps the shared-memory dequant kernels.
-  if (w8 && peers.n == 0 && (m >= kTwoPassMinTokens || use_w8t_short() || use_w8t()) &&
+  // Narrow matrices (<= 1024 outputs) at 129..2048 tokens stay on the
+  // shared-memory dequant kernel, measured faster there (few weight tiles:
+  // the tokens-as-M tiling spreads them over more SMs).
+  // B200_GEMM_W8T_NARROW=1 sends them to the TMEM-weight kernel.
+  const char* nv = getenv("B200_GEMM_W8T_NARROW");
+  const bool narrow = m > 128 && m <= 2048 && n <= 1024 && !(nv != nullptr && nv[0] == '1');
+  if (w8 && peers.n == 0 && !narrow &&
+      (m >= kTwoPassMinTokens || use_w8t_short() || use_w8t()) &&
       gemm_w8t_supported(weight, input, output, m, n, k)) {
     return launch_gemm_w8t(weight, scales, bias, input, output, m, n, k, ldc, stream);
   }
