@@ -124,7 +124,8 @@ struct Spin {
   int n = 0;
 };
 __device__ __forceinline__ bool spin_on(Spin& s, const PersistArgs& a, const Smem& sm) {
-  __nanosleep(64);  // eases the polling load on the L2 lines being written
+  // No sleep between polls: with __nanosleep(64) here decode ran at 2157
+  // tok/s, without it 2241 (input staging 1.0 -> 0.67 us per phase).
   if ((++s.n & 31) != 0) return true;
   if (*reinterpret_cast<volatile int*>(a.grid_abort) != 0 || *sm.abort_flag != 0) {
     *sm.abort_flag = 1;
