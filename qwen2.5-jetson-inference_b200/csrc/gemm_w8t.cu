@@ -1201,6 +1201,22 @@ cudaError_t launch_split_bt(const void* weight, const bf16* scales, const bf16* 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  // A cluster of `splits` CTAs must fit on the device (checked once per
+  // device and cluster size); otherwise the caller takes the unsplit kernel
+  // instead of a launch that would fail.
+  static std::atomic<int> fits[64][9];  // 0 unknown, 1 fits, 2 does not
+  if (dev >= 0 && dev < 64 && splits <= 8) {
+    int f = fits[dev][splits].load(std::memory_order_relaxed);
+    if (f == 0) {
+      int clusters = 0;
+      const cudaError_t e = cudaOccupancyMaxActiveClusters(
+          &clusters, gemm_w8t_split_kernel<kBT, kW16>, &cfg);
+      if (e != cudaSuccess) cudaGetLastError();
+      f = (e == cudaSuccess && clusters >= 1) ? 1 : 2;
+      fits[dev][splits].store(f, std::memory_order_relaxed);
+    }
+    if (f == 2) return cudaErrorNotSupported;
+  }
   return cudaLaunchKernelEx(&cfg, gemm_w8t_split_kernel<kBT, kW16>, tx, tq,
                             reinterpret_cast<const uint16_t*>(scales), bias, output, m, n, k,
                             ldc);
