@@ -415,3 +415,45 @@ def test_cluster_split_k(b200, oracle, cuda, m, k, n, w8):
     assert np.all(np.abs(got - exp) <= np.abs(exp) * 2.0 ** -7 * 1.01 + 1e-4)
     unsplit = oracle.bf16_to_f32(to_bits(ys[2]))
     assert np.all(np.abs(got - unsplit) <= np.abs(unsplit) * 2.0 ** -7 * 1.01 + 1e-4)
+
+
+@pytest.mark.parametrize("w8", [True, False], ids=["w8a16", "bf16"])
+def test_full_size_prefill_every_output(b200, cuda, w8):
+    """configs[2]'s largest case, 8192 x 896 -> 151936 (1.24 G outputs), every
+    output against a torch FP32 product of X with the GEMM's weights (BF16 W,
+    or bf16(q * s) for W8A16), TF32 off, computed in row blocks: each within
+    one BF16 ulp of the FP32 value (plus 1e-4 absolute)."""
+    import torch
+    m, k, n = 8192, 896, 151936
+    g = torch.Generator(device=cuda)
+    g.manual_seed(8192)
+    w = torch.randn(n, k, generator=g, device=cuda) * 0.02
+    bias = (torch.randn(n, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g, device=cuda).to(torch.bfloat16)
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    if w8:
+        q, s = b200.quantize_groupwise(w)
+        b200.gemm_w8a16(q, s, 64, bias, x, y, m, n, k)
+        wd = (q.float() * s.float().repeat_interleave(64, dim=1)).to(torch.bfloat16).float()
+        del q, s
+    else:
+        wb = w.to(torch.bfloat16)
+        b200.gemm_bf16(wb, bias, x, y, m, n, k)
+        wd = wb.float()
+        del wb
+    del w
+    torch.cuda.synchronize()
+    assert b200.device_status() == 0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        bad = 0
+        for r0 in range(0, m, 1024):
+            ref = x[r0:r0 + 1024].float() @ wd.t() + bias.float()
+            got = y[r0:r0 + 1024].float()
+            tol = ref.abs() * 2.0 ** -7 * 1.01 + 1e-4
+            bad += int(((got - ref).abs() > tol).sum())
+            del ref, got, tol
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert bad == 0, f"{bad} outputs off"
